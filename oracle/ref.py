@@ -1,0 +1,170 @@
+"""Python front end of the CPU oracle for MhcPre -- TEST INFRASTRUCTURE ONLY.
+
+``mhc_pre_ref`` calls the C restatement in ``mhc_pre_oracle.c`` (see its header for
+the formula and the reference lines it follows).  ``mhc_pre_numpy`` is an
+independent float64 restatement used to cross-check the C oracle: it follows
+cloud_runner/runner.cpp:122-192 (double square-sum) with float64 everywhere
+else, so it is "truth" up to the final fp32/16-bit rounding of the outputs.
+
+x and hIn are 16-bit patterns (np.uint16) of the x dtype ("fp16" or "bf16").
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+_LIB_PATH = _HERE / "libmhc_oracle.so"
+_lib = None
+
+ORDER_KERNEL = 0
+ORDER_AUDIT = 1
+DTYPE_CODE = {"fp16": 0, "bf16": 1}
+
+
+def build(force: bool = False) -> Path:
+    """Compile the C oracle in place (gcc + OpenMP)."""
+    src = _HERE / "mhc_pre_oracle.c"
+    if force or not _LIB_PATH.exists() or _LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        subprocess.check_call(["make", "-s", "-C", str(_HERE), "libmhc_oracle.so"])
+    return _LIB_PATH
+
+
+def _load():
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            build()
+        lib = ctypes.CDLL(str(_LIB_PATH))
+        u16p = ctypes.POINTER(ctypes.c_uint16)
+        f32p = ctypes.POINTER(ctypes.c_float)
+        lib.mhc_pre_oracle.restype = ctypes.c_int
+        lib.mhc_pre_oracle.argtypes = [
+            ctypes.c_int64, ctypes.c_int, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+            u16p, f32p, f32p, f32p, f32p, ctypes.c_float, ctypes.c_float,
+            u16p, f32p, f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int]
+        lib.mhc_oracle_f32_to_f16.restype = ctypes.c_uint16
+        lib.mhc_oracle_f32_to_f16.argtypes = [ctypes.c_float]
+        lib.mhc_oracle_f32_to_bf16.restype = ctypes.c_uint16
+        lib.mhc_oracle_f32_to_bf16.argtypes = [ctypes.c_float]
+        lib.mhc_oracle_f16_to_f32.restype = ctypes.c_float
+        lib.mhc_oracle_f16_to_f32.argtypes = [ctypes.c_uint16]
+        lib.mhc_oracle_bf16_to_f32.restype = ctypes.c_float
+        lib.mhc_oracle_bf16_to_f32.argtypes = [ctypes.c_uint16]
+        lib.mhc_oracle_max_threads.restype = ctypes.c_int
+        _lib = lib
+    return _lib
+
+
+def _ptr(a: np.ndarray, ctype):
+    return a.ctypes.data_as(ctypes.POINTER(ctype))
+
+
+def max_threads() -> int:
+    return int(_load().mhc_oracle_max_threads())
+
+
+def f32_to_f16_bits(v: float) -> int:
+    return int(_load().mhc_oracle_f32_to_f16(ctypes.c_float(v)))
+
+
+def f32_to_bf16_bits(v: float) -> int:
+    return int(_load().mhc_oracle_f32_to_bf16(ctypes.c_float(v)))
+
+
+def f16_bits_to_f32(b: int) -> float:
+    return float(_load().mhc_oracle_f16_to_f32(b))
+
+
+def bf16_bits_to_f32(b: int) -> float:
+    return float(_load().mhc_oracle_bf16_to_f32(b))
+
+
+def to_float(bits: np.ndarray, dtype: str) -> np.ndarray:
+    """Decode 16-bit patterns to float32 (vectorised, exact)."""
+    bits = np.asarray(bits, dtype=np.uint16)
+    if dtype == "bf16":
+        return (bits.astype(np.uint32) << 16).view(np.float32)
+    return bits.view(np.float16).astype(np.float32)
+
+
+def from_float(values: np.ndarray, dtype: str) -> np.ndarray:
+    """Round float32 values to 16-bit patterns, nearest even (vectorised)."""
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    if dtype == "bf16":
+        u = v.view(np.uint32).astype(np.uint64)
+        lsb = (u >> 16) & 1
+        return (((u + 0x7FFF + lsb) & 0xFFFF0000) >> 16).astype(np.uint16)
+    return v.astype(np.float16).view(np.uint16)
+
+
+def mhc_pre_ref(x_bits, phi, alpha, bias, gamma, n: int, D: int, dtype: str,
+                norm_eps: float = 1e-6, hc_eps: float = 1e-6, order: int = ORDER_KERNEL,
+                rows: tuple[int, int] | None = None, threads: int = 0):
+    """Run the C oracle.  x_bits: uint16 [M, n, D] (or [M, n*D]); phi: float32 [mix, n*D].
+
+    Returns (hIn_bits uint16 [R, D], hPost float32 [R, n], hRes float32 [R, n, n]) for
+    rows [r0, r1) (all rows by default)."""
+    lib = _load()
+    K = n * D
+    mix = n * n + 2 * n
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16).reshape(-1, K)
+    M = x_bits.shape[0]
+    phi = np.ascontiguousarray(phi, dtype=np.float32).reshape(mix, K)
+    alpha = np.ascontiguousarray(alpha, dtype=np.float32).reshape(3)
+    bias = np.ascontiguousarray(bias, dtype=np.float32).reshape(mix)
+    g = None if gamma is None else np.ascontiguousarray(gamma, dtype=np.float32).reshape(K)
+    r0, r1 = (0, M) if rows is None else rows
+    hIn = np.zeros((M, D), dtype=np.uint16)
+    hPost = np.zeros((M, n), dtype=np.float32)
+    hRes = np.zeros((M, n, n), dtype=np.float32)
+    f32p = ctypes.c_float
+    rc = lib.mhc_pre_oracle(
+        M, n, D, DTYPE_CODE[dtype], order,
+        _ptr(x_bits, ctypes.c_uint16), _ptr(phi, f32p), _ptr(alpha, f32p), _ptr(bias, f32p),
+        None if g is None else _ptr(g, f32p), norm_eps, hc_eps,
+        _ptr(hIn, ctypes.c_uint16), _ptr(hPost, f32p), _ptr(hRes, f32p), r0, r1, threads)
+    if rc != 0:
+        raise RuntimeError(f"mhc_pre_oracle failed with code {rc}")
+    return hIn[r0:r1], hPost[r0:r1], hRes[r0:r1]
+
+
+def mhc_pre_numpy(x_bits, phi, alpha, bias, gamma, n: int, D: int, dtype: str,
+                  norm_eps: float = 1e-6, hc_eps: float = 1e-6):
+    """float64 restatement (vectorised over rows); returns float64 hIn (before the
+    16-bit rounding), hPost, hRes and hPre."""
+    K = n * D
+    mix = n * n + 2 * n
+    xf = to_float(np.asarray(x_bits).reshape(-1, K), dtype).astype(np.float64)
+    sumsq = (xf * xf).sum(axis=1)
+    inv_rms = 1.0 / np.sqrt(sumsq / K + norm_eps)
+    xg = xf * (np.asarray(gamma, np.float64).reshape(1, K) if gamma is not None else 1.0)
+    mixv = xg @ np.asarray(phi, np.float64).reshape(mix, K).T
+    scaled = mixv * inv_rms[:, None]
+    a = np.asarray(alpha, np.float64)
+    b = np.asarray(bias, np.float64)
+    h_pre = 1.0 / (1.0 + np.exp(-(scaled[:, :n] * a[0] + b[:n]))) + hc_eps
+    h_post = 2.0 / (1.0 + np.exp(-(scaled[:, n:2 * n] * a[1] + b[n:2 * n])))
+    h_res = (scaled[:, 2 * n:] * a[2] + b[2 * n:]).reshape(-1, n, n)
+    xs = xf.reshape(-1, n, D)
+    h_in = np.einsum("rs,rsd->rd", h_pre, xs)
+    return h_in, h_post, h_res, h_pre
+
+
+def ulp_distance(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
+    """Distance in units of the last place between two arrays of 16-bit float
+    patterns (fp16 or bf16: both are sign-magnitude with the exponent above the
+    mantissa, so ordering the magnitudes works for either)."""
+    def ordered(bits):
+        b = np.asarray(bits, dtype=np.uint16).astype(np.int32)
+        mag = b & 0x7FFF
+        return np.where(b & 0x8000, -mag, mag)
+    return np.abs(ordered(a_bits) - ordered(b_bits))
+
+
+if __name__ == "__main__":  # pragma: no cover
+    print(build(force=True), max_threads(), os.cpu_count())
