@@ -16,9 +16,12 @@
 static inline uint32_t f32_bits(float v) { uint32_t b; memcpy(&b, &v, 4); return b; }
 static inline float bits_f32(uint32_t b) { float v; memcpy(&v, &b, 4); return v; }
 
-/* fp32 -> fp16 bits, round to nearest even, subnormals and overflow handled as in
- * audit_group_vec.py:162-191 (NaN keeps a quiet payload bit of 1). */
-uint16_t mhc_oracle_f32_to_f16(float value)
+/* fp32 -> fp16 bits, IEEE round to nearest even (subnormals, overflow to inf;
+ * NaN keeps a quiet payload bit of 1).  `audit_carry` reproduces a quirk of the
+ * reference's helper (audit_group_vec.py:181, cloud_runner/runner.cpp:85): it
+ * masks the rounded subnormal with 0x3FF, so a value just below the smallest
+ * normal (2^-14) that rounds up to it becomes 0 instead of 2^-14. */
+static uint16_t f32_to_f16_impl(float value, int audit_carry)
 {
     const uint32_t v = f32_bits(value);
     const uint32_t sign = (v >> 16) & 0x8000u;
@@ -43,7 +46,7 @@ uint16_t mhc_oracle_f32_to_f16(float value)
         if (rem > tie || (rem == tie && (half & 1u))) {
             half++;
         }
-        return (uint16_t)(sign | (half & 0x3FFu));
+        return (uint16_t)(sign | (audit_carry ? (half & 0x3FFu) : half));
     }
     uint32_t m16 = mant >> 13;
     const uint32_t rem = mant & 0x1FFFu;
@@ -59,6 +62,9 @@ uint16_t mhc_oracle_f32_to_f16(float value)
     }
     return (uint16_t)(sign | ((uint32_t)e16 << 10) | m16);
 }
+
+uint16_t mhc_oracle_f32_to_f16(float value) { return f32_to_f16_impl(value, 0); }
+uint16_t mhc_oracle_f32_to_f16_audit(float value) { return f32_to_f16_impl(value, 1); }
 
 /* fp32 -> bf16 bits: add 0x7FFF plus the kept LSB, truncate
  * (audit_group_vec.py:209-213, cloud_runner/runner.cpp:102-108). */
@@ -107,9 +113,12 @@ static inline float load_x(const uint16_t *p, int dtype)
     return dtype == MHC_ORACLE_BF16 ? mhc_oracle_bf16_to_f32(*p) : mhc_oracle_f16_to_f32(*p);
 }
 
-static inline uint16_t store_x(float v, int dtype)
+static inline uint16_t store_x(float v, int dtype, int order)
 {
-    return dtype == MHC_ORACLE_BF16 ? mhc_oracle_f32_to_bf16(v) : mhc_oracle_f32_to_f16(v);
+    if (dtype == MHC_ORACLE_BF16) {
+        return mhc_oracle_f32_to_bf16(v);
+    }
+    return order == MHC_ORACLE_ORDER_AUDIT ? mhc_oracle_f32_to_f16_audit(v) : mhc_oracle_f32_to_f16(v);
 }
 
 /* The Ascend kernel's vector tile for the square-sum (code/op_host/mhc_pre.cpp:11). */
@@ -283,7 +292,7 @@ int mhc_pre_oracle(int64_t M, int n, int64_t D, int dtype, int order,
                         a = a + p;
                     }
                 }
-                hIn[r * D + d] = store_x(a, dtype);
+                hIn[r * D + d] = store_x(a, dtype, order);
             }
         }
         free(xf);
@@ -291,4 +300,25 @@ int mhc_pre_oracle(int64_t M, int n, int64_t D, int dtype, int order,
     }
     free(phiT);
     return failed ? -2 : 0;
+}
+
+/* Inputs of the reference's E3 shape-matrix runner, drawn with the C library's
+ * rand() exactly as cloud_runner/runner.cpp:370-382 does after srand(seed):
+ * x, then phi ([mix][K] order), then bias, then gamma (always drawn). */
+void mhc_oracle_runner_inputs(unsigned seed, int64_t nx, int64_t nphi, int64_t nbias, int64_t ngamma,
+                              float *x, float *phi, float *bias, float *gamma)
+{
+    srand(seed);
+    for (int64_t i = 0; i < nx; ++i) {
+        x[i] = (float)(rand() % 2000) / 10000.0f - 0.1f;
+    }
+    for (int64_t i = 0; i < nphi; ++i) {
+        phi[i] = (float)(rand() % 200) / 10000.0f - 0.01f;
+    }
+    for (int64_t i = 0; i < nbias; ++i) {
+        bias[i] = (float)(rand() % 200) / 10000.0f - 0.01f;
+    }
+    for (int64_t i = 0; i < ngamma; ++i) {
+        gamma[i] = 1.0f + (float)(rand() % 200) / 10000.0f;
+    }
 }

@@ -23,8 +23,9 @@
  *       Muls/Add/Muls(-1)/Exp/Adds(1)/Div/Adds(eps) (:542-555),
  *       hIn = Brcb mul then (x0+x1)+x2... (:91-222, :793-812).
  *   MHC_ORACLE_ORDER_AUDIT   follows audit_group_vec.py:279-324 exactly
- *       (sequential fp32 square-sum, double sqrt/exp/eps adds, (mix*invRms)*alpha);
- *       it reproduces the audit's outputs bit for bit.
+ *       (sequential fp32 square-sum, double sqrt/exp/eps adds, (mix*invRms)*alpha,
+ *       the helper's fp16 subnormal-carry quirk); it reproduces the audit's
+ *       outputs bit for bit.
  * The GEMM accumulates sequentially over k in fp32 in both orders
  * (audit_group_vec.py:243-252; cloud_runner/runner.cpp:155-158).
  */
@@ -49,12 +50,20 @@ int mhc_pre_oracle(int64_t M, int n, int64_t D, int dtype, int order,
                    uint16_t *hIn, float *hPost, float *hRes,
                    int64_t row_begin, int64_t row_end, int threads);
 
-/* Bit-level conversion helpers (round to nearest even), matching
- * audit_group_vec.py:162-213 and cloud_runner/runner.cpp:45-116. */
+/* Bit-level conversion helpers (IEEE round to nearest even), the conversions of
+ * audit_group_vec.py:162-213 and cloud_runner/runner.cpp:45-116.  The _audit
+ * variant keeps the reference helper's subnormal-carry quirk (it maps values
+ * that round up to the smallest normal, 2^-14, to zero); the audit order uses
+ * it for hIn so that the oracle reproduces the audit bit for bit. */
 uint16_t mhc_oracle_f32_to_f16(float v);
+uint16_t mhc_oracle_f32_to_f16_audit(float v);
 uint16_t mhc_oracle_f32_to_bf16(float v);
 float mhc_oracle_f16_to_f32(uint16_t h);
 float mhc_oracle_bf16_to_f32(uint16_t b);
+
+/* Inputs of the reference's E3 runner (cloud_runner/runner.cpp:370-382). */
+void mhc_oracle_runner_inputs(unsigned seed, int64_t nx, int64_t nphi, int64_t nbias, int64_t ngamma,
+                              float *x, float *phi, float *bias, float *gamma);
 
 /* Number of OpenMP threads the oracle would use (for reporting). */
 int mhc_oracle_max_threads(void);

@@ -49,6 +49,8 @@ def _load():
             u16p, f32p, f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int]
         lib.mhc_oracle_f32_to_f16.restype = ctypes.c_uint16
         lib.mhc_oracle_f32_to_f16.argtypes = [ctypes.c_float]
+        lib.mhc_oracle_f32_to_f16_audit.restype = ctypes.c_uint16
+        lib.mhc_oracle_f32_to_f16_audit.argtypes = [ctypes.c_float]
         lib.mhc_oracle_f32_to_bf16.restype = ctypes.c_uint16
         lib.mhc_oracle_f32_to_bf16.argtypes = [ctypes.c_float]
         lib.mhc_oracle_f16_to_f32.restype = ctypes.c_float
@@ -56,12 +58,32 @@ def _load():
         lib.mhc_oracle_bf16_to_f32.restype = ctypes.c_float
         lib.mhc_oracle_bf16_to_f32.argtypes = [ctypes.c_uint16]
         lib.mhc_oracle_max_threads.restype = ctypes.c_int
+        lib.mhc_oracle_runner_inputs.restype = None
+        lib.mhc_oracle_runner_inputs.argtypes = [ctypes.c_uint, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                 ctypes.c_int64, f32p, f32p, f32p, f32p]
         _lib = lib
     return _lib
 
 
 def _ptr(a: np.ndarray, ctype):
     return a.ctypes.data_as(ctypes.POINTER(ctype))
+
+
+def runner_inputs(M: int, n: int, D: int, seed: int = 42):
+    """The reference E3 runner's inputs (cloud_runner/runner.cpp:368-382) as fp32
+    arrays: x [M, n*D], phi [mix, n*D], bias [mix], gamma [n*D], alpha [3]."""
+    lib = _load()
+    K = n * D
+    mix = n * n + 2 * n
+    x = np.empty(M * K, np.float32)
+    phi = np.empty(mix * K, np.float32)
+    bias = np.empty(mix, np.float32)
+    gamma = np.empty(K, np.float32)
+    f = ctypes.c_float
+    lib.mhc_oracle_runner_inputs(seed, x.size, phi.size, bias.size, gamma.size, _ptr(x, f), _ptr(phi, f),
+                                 _ptr(bias, f), _ptr(gamma, f))
+    alpha = np.array([0.5, 0.3, 0.2], np.float32)
+    return x.reshape(M, K), phi.reshape(mix, K), bias, gamma, alpha
 
 
 def max_threads() -> int:
@@ -92,14 +114,22 @@ def to_float(bits: np.ndarray, dtype: str) -> np.ndarray:
     return bits.view(np.float16).astype(np.float32)
 
 
-def from_float(values: np.ndarray, dtype: str) -> np.ndarray:
-    """Round float32 values to 16-bit patterns, nearest even (vectorised)."""
+def from_float(values: np.ndarray, dtype: str, audit_carry: bool = False) -> np.ndarray:
+    """Round float32 values to 16-bit patterns, IEEE nearest even (vectorised).
+
+    audit_carry=True reproduces the reference helper's fp16 quirk
+    (audit_group_vec.py:181): a subnormal that rounds up to the smallest normal
+    (2^-14) becomes zero."""
     v = np.ascontiguousarray(values, dtype=np.float32)
     if dtype == "bf16":
         u = v.view(np.uint32).astype(np.uint64)
         lsb = (u >> 16) & 1
         return (((u + 0x7FFF + lsb) & 0xFFFF0000) >> 16).astype(np.uint16)
-    return v.astype(np.float16).view(np.uint16)
+    b = v.astype(np.float16).view(np.uint16)
+    if audit_carry:
+        carried = ((b & 0x7FFF) == 0x0400) & (np.abs(v) < np.float32(2.0 ** -14))
+        b = np.where(carried, b & 0x8000, b).astype(np.uint16)
+    return b
 
 
 def mhc_pre_ref(x_bits, phi, alpha, bias, gamma, n: int, D: int, dtype: str,
@@ -153,6 +183,15 @@ def mhc_pre_numpy(x_bits, phi, alpha, bias, gamma, n: int, D: int, dtype: str,
     xs = xf.reshape(-1, n, D)
     h_in = np.einsum("rs,rsd->rd", h_pre, xs)
     return h_in, h_post, h_res, h_pre
+
+
+def ulp_size(bits: np.ndarray, dtype: str) -> np.ndarray:
+    """Spacing between the magnitude of each 16-bit value and the next larger one."""
+    mag = np.asarray(bits, dtype=np.uint16) & 0x7FFF
+    top = 0x7BFF if dtype == "fp16" else 0x7F7F
+    lo = np.minimum(mag, top - 1).astype(np.uint16)
+    hi = (lo + 1).astype(np.uint16)
+    return (to_float(hi, dtype).astype(np.float64) - to_float(lo, dtype).astype(np.float64))
 
 
 def ulp_distance(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:

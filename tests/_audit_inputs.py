@@ -35,7 +35,7 @@ def audit_inputs(n: int, d: int, has_gamma: bool, dtype: str, rows: int, seed: i
     v = lehmer_values(seed, count)
     pos = 0
     x32 = (v[pos:pos + rows * flat] * 0.5).astype(np.float32); pos += rows * flat
-    x_bits = from_float(x32, dtype).reshape(rows, flat)
+    x_bits = from_float(x32, dtype, audit_carry=True).reshape(rows, flat)
     phi = (v[pos:pos + mix * flat] * 0.1).astype(np.float32).reshape(mix, flat); pos += mix * flat
     gamma = None
     if has_gamma:

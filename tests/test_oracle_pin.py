@@ -32,6 +32,27 @@ def test_reference_bf16_known_answer():
     assert ref.from_float(np.array([0.1], np.float32), "bf16")[0] == b
 
 
+def test_fp16_subnormal_carry_quirk_of_reference_helper():
+    """The reference's fp16 helper (audit_group_vec.py:181, runner.cpp:85) drops the
+    carry when a subnormal rounds up to the smallest normal 2^-14; the device cast
+    (CAST_RINT, and CUDA's __float2half_rn) rounds correctly.  The oracle keeps the
+    quirk only in audit order."""
+    import ctypes
+    L = ref._load()
+    rng = np.random.default_rng(1)
+    vals = np.concatenate([rng.uniform(-1e-4, 1e-4, 50000), rng.uniform(-2, 2, 50000),
+                           np.float32(2.0 ** -14) * (1 - rng.uniform(0, 1e-3, 2000))]).astype(np.float32)
+    ieee = ref.from_float(vals, "fp16")
+    quirk = ref.from_float(vals, "fp16", audit_carry=True)
+    c_ieee = np.array([L.mhc_oracle_f32_to_f16(ctypes.c_float(v)) for v in vals], np.uint16)
+    c_quirk = np.array([L.mhc_oracle_f32_to_f16_audit(ctypes.c_float(v)) for v in vals], np.uint16)
+    assert np.array_equal(c_ieee, ieee)
+    assert np.array_equal(c_quirk, quirk)
+    assert np.array_equal(ieee, vals.astype(np.float16).view(np.uint16))
+    differs = ieee != quirk
+    assert differs.sum() > 0 and np.all((ieee[differs] & 0x7FFF) == 0x0400) and np.all((quirk[differs] & 0x7FFF) == 0)
+
+
 def test_half_conversions_roundtrip_exhaustive():
     bits = np.arange(0, 1 << 16, dtype=np.uint32).astype(np.uint16)
     f16 = ref.to_float(bits, "fp16")
