@@ -1,0 +1,157 @@
+/*
+ * mhc_pre.h -- C ABI of the B200-native MhcPre operator (libmhcpre_b200.so).
+ *
+ * MhcPre is the "pre" half of a manifold-constrained hyper-connection block.
+ * For every token row r of x [B, S, n, D] (n in {4, 6, 8}, K = n*D,
+ * mix = n*n + 2n):
+ *
+ *   invRms[r] = 1 / sqrt(sum_k x[r,k]^2 / K + normEps)      raw x, before gamma
+ *   mix[r,j]  = sum_k x[r,k] * gamma[k] * phi[j,k]           phi stored [mix][K]
+ *   hPre[r,s] = sigmoid(mix[r,s] * invRms * alpha[0] + bias[s]) + hcEps
+ *   hPost     = 2 * sigmoid(mix[r,n+s] * invRms * alpha[1] + bias[n+s])   -> output
+ *   hRes      = mix[r,2n+i] * invRms * alpha[2] + bias[2n+i]             -> output
+ *   hIn[r,d]  = round_to_x_dtype(((hPre0*x0[d] + hPre1*x1[d]) + hPre2*x2[d]) + ...)
+ *
+ * It replaces the reference's generated two-phase aclnn API
+ * (ZXY-0508/MhcPre-review, OpDef at code/op_host/mhc_pre.cpp:261-304, called at
+ * cloud_runner/runner.cpp:443-472):
+ *
+ *   aclnnMhcPreGetWorkspaceSize(x, phi, alpha, bias, gamma, normEps, hcEps,
+ *                               hIn, hPost, hRes, &workspaceSize, &executor)
+ *   aclnnMhcPre(workspace, workspaceSize, executor, stream)
+ *
+ * Conventions (same as the reference):
+ *   - the caller allocates every device buffer and the workspace; the operator
+ *     writes only hIn, hPost, hRes and the workspace;
+ *   - calls are asynchronous on the given CUDA stream (a cudaStream_t passed as
+ *     void*; NULL is the legacy default stream) and never synchronize;
+ *   - 0 means success, negative values are errors (see mhcStatus_t);
+ *   - there is no global mutable host state: calls are reentrant and thread-safe
+ *     (the reference keeps an unlocked 4-slot tiling cache, mhc_pre.cpp:51).
+ * x, hIn and the workspace must be 16-byte aligned, the fp32 tensors 4-byte
+ * aligned; all tensors are dense row-major.
+ */
+#ifndef MHC_PRE_H
+#define MHC_PRE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MHC_PRE_ABI_VERSION 1
+
+/* Exported entry points keep default visibility even when the library is
+ * built with -fvisibility=hidden. */
+#if defined(__GNUC__)
+#define MHC_API __attribute__((visibility("default")))
+#else
+#define MHC_API
+#endif
+
+/* Data type of x and hIn (the reference's template key DT_X,
+ * code/op_kernel/tiling_key_mhc_pre.h:6-13). */
+typedef enum {
+    MHC_DTYPE_F16 = 0,
+    MHC_DTYPE_BF16 = 1
+} mhcDtype_t;
+
+typedef enum {
+    MHC_STATUS_SUCCESS = 0,
+    MHC_STATUS_NULL_POINTER = -1,        /* a required pointer is NULL */
+    MHC_STATUS_BAD_SHAPE = -2,           /* B, S or D <= 0 (TilingFunc, mhc_pre.cpp:76-78) */
+    MHC_STATUS_BAD_STREAM_COUNT = -3,    /* n not in {4, 6, 8} (mhc_pre.cpp:77) */
+    MHC_STATUS_BAD_HEAD_DIM = -4,        /* D % 16 != 0 or n*D % 8 != 0 (mhc_pre.cpp:127-128) */
+    MHC_STATUS_MIX_TOO_LARGE = -5,       /* n*n + 2n > 80 (mhc_pre.cpp:127) */
+    MHC_STATUS_BAD_DTYPE = -6,           /* dtype not F16/BF16 (OpDef, mhc_pre.cpp:265-268) */
+    MHC_STATUS_MISALIGNED = -7,          /* a device pointer violates the alignment rule above */
+    MHC_STATUS_WORKSPACE_TOO_SMALL = -8, /* workspace smaller than mhcPreGetWorkspaceSize */
+    MHC_STATUS_CUDA_ERROR = -9,          /* a CUDA runtime/driver call failed */
+    MHC_STATUS_UNSUPPORTED_DEVICE = -10, /* current device is not sm_100 */
+    MHC_STATUS_DEVICE_TIMEOUT = -11,     /* a kernel gave up a bounded wait (see mhcPreGetDeviceStatus) */
+    MHC_STATUS_NOT_PREPARED = -12,       /* mhcPreRunPrepared on a workspace without prepared weights */
+    MHC_STATUS_TOO_LARGE = -13           /* problem exceeds a documented size limit */
+} mhcStatus_t;
+
+/* Problem description: the shape/attribute part of the aclnn executor.
+ * x is [batch, seq, streams, headDim]; gamma is optional ([streams, headDim]).
+ * normEps/hcEps are the OpDef attributes (default 1e-6, mhc_pre.cpp:297-298). */
+typedef struct {
+    int64_t batch;
+    int64_t seq;
+    int64_t streams;
+    int64_t headDim;
+    int32_t dtype;    /* mhcDtype_t */
+    int32_t hasGamma; /* 0 or 1 */
+    float normEps;
+    float hcEps;
+} mhcPreDesc_t;
+
+/* Validates the description (same rejects as the reference TilingFunc,
+ * mhc_pre.cpp:57-79, :126-129) and returns the workspace size in bytes for the
+ * current CUDA device.  Replaces aclnnMhcPreGetWorkspaceSize. */
+MHC_API int mhcPreGetWorkspaceSize(const mhcPreDesc_t* desc, size_t* workspaceBytes);
+
+/* Prepares the weights into the workspace: phi'[j,k] = gamma[k]*phi[j,k] split
+ * into a high and a low 16-bit part of the x dtype, laid out for the tensor
+ * cores.  phi is fp32 [mix][K] (the reference's phi layout, K-contiguous; see
+ * cloud_runner/runner.cpp:157); gamma is fp32 [K] or NULL when hasGamma == 0.
+ * After this call, mhcPreRunPrepared may be called any number of times with the
+ * same workspace.  No reference counterpart: the reference re-reads fp32 phi on
+ * every launch (mhc_pre.cpp:535). */
+MHC_API int mhcPrePrepareWeights(const mhcPreDesc_t* desc, const float* phi, const float* gamma, void* workspace,
+                                 size_t workspaceBytes, void* stream);
+
+/* One-shot operator call: prepares the weights and runs the operator.
+ * x: [B,S,n,D] f16/bf16; phi: fp32 [mix][K]; alpha: fp32 [3] (pre, post, res);
+ * bias: fp32 [mix]; gamma: fp32 [K] or NULL; hIn: [B,S,D] x dtype;
+ * hPost: fp32 [B,S,n]; hRes: fp32 [B,S,n,n].
+ * Replaces aclnnMhcPreGetWorkspaceSize + aclnnMhcPre (runner.cpp:443-472). */
+MHC_API int mhcPreRun(const mhcPreDesc_t* desc, const void* x, const float* phi, const float* alpha,
+                      const float* bias, const float* gamma, void* hIn, float* hPost, float* hRes, void* workspace,
+                      size_t workspaceBytes, void* stream);
+
+/* Runs the operator with weights prepared earlier by mhcPrePrepareWeights into
+ * the same workspace (relaunching the same executor, probe_e1e2.cpp:312-318). */
+MHC_API int mhcPreRunPrepared(const mhcPreDesc_t* desc, const void* x, const float* alpha, const float* bias,
+                              void* hIn, float* hPost, float* hRes, void* workspace, size_t workspaceBytes,
+                              void* stream);
+
+/* mhcPreRunPrepared that also records two caller-created CUDA events (cudaEvent_t
+ * passed as void*, either may be NULL) on the stream immediately before and after
+ * the operator's main kernel, so a caller can time that kernel alone inside a
+ * longer loop.  Profiling aid; no reference counterpart. */
+MHC_API int mhcPreRunPreparedProfiled(const mhcPreDesc_t* desc, const void* x, const float* alpha, const float* bias,
+                                      void* hIn, float* hPost, float* hRes, void* workspace, size_t workspaceBytes,
+                                      void* stream, void* mainKernelBegin, void* mainKernelEnd);
+
+/* Execution plan chosen for a description on the current device (for tests,
+ * benchmarks and profiling; no reference counterpart). */
+typedef struct {
+    int32_t path;           /* 0 = split-K GEMM + epilogue kernels, 1 = fused single kernel */
+    int32_t kernelsPerRun;  /* kernels launched by mhcPreRunPrepared */
+    int32_t gridCtas;       /* CTAs of the main kernel */
+    int32_t splits;         /* K splits (path 0) or team size (path 1) */
+    int32_t rowsPerTile;    /* token rows per tensor-core tile */
+    int32_t reserved[3];
+} mhcPrePlan_t;
+
+MHC_API int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* plan);
+
+/* Reads and clears the device-side error word of the current device (set when
+ * a kernel gave up a bounded wait).  Synchronizes the current device.
+ * *deviceStatus receives 0 or a negative mhcStatus_t. */
+MHC_API int mhcPreGetDeviceStatus(int32_t* deviceStatus);
+
+/* Human-readable name of a status code (static string). */
+MHC_API const char* mhcPreStatusString(int status);
+
+/* MHC_PRE_ABI_VERSION of the loaded library. */
+MHC_API int mhcPreAbiVersion(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MHC_PRE_H */

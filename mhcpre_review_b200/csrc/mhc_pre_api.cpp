@@ -1,0 +1,280 @@
+// C ABI of the MhcPre operator (declared in include/mhc_pre.h).
+//
+// This layer mirrors the reference host op (code/op_host/mhc_pre.cpp):
+//   - the same shape rejects as TilingFunc (:57-79, :126-129),
+//   - the InferShape output shapes (:217-249) are implied by the description,
+//   - a workspace sized on the host, owned by the caller (:183-190),
+// and replaces the Ascend tiling (core split, M64 matmul tiling, tiling cache)
+// with a B200 launch plan.  It keeps no mutable global state.
+#include <algorithm>
+#include <cstring>
+
+#include "mhc_pre_internal.h"
+
+namespace mhc {
+
+static uint32_t fnv1a(const void* data, size_t n, uint32_t h = 2166136261u) {
+    const auto* b = static_cast<const uint8_t*>(data);
+    for (size_t i = 0; i < n; ++i) {
+        h ^= b[i];
+        h *= 16777619u;
+    }
+    return h;
+}
+
+int make_problem(const mhcPreDesc_t* desc, Problem* p) {
+    if (desc == nullptr || p == nullptr) return MHC_STATUS_NULL_POINTER;
+    if (desc->batch <= 0 || desc->seq <= 0 || desc->headDim <= 0) return MHC_STATUS_BAD_SHAPE;
+    if (desc->streams != 4 && desc->streams != 6 && desc->streams != 8) return MHC_STATUS_BAD_STREAM_COUNT;
+    if (desc->dtype != MHC_DTYPE_F16 && desc->dtype != MHC_DTYPE_BF16) return MHC_STATUS_BAD_DTYPE;
+    const int64_t n = desc->streams;
+    const int64_t mix = n * n + 2 * n;
+    if (mix > kMaxMix) return MHC_STATUS_MIX_TOO_LARGE;
+    if (desc->headDim % 16 != 0 || (n * desc->headDim) % 8 != 0) return MHC_STATUS_BAD_HEAD_DIM;
+    // TMA coordinates and the row index of the tile grid are 32-bit.
+    if (desc->batch > (int64_t(1) << 31) / desc->seq) return MHC_STATUS_TOO_LARGE;
+    const int64_t M = desc->batch * desc->seq;
+    const int64_t K = n * desc->headDim;
+    if (K >= (int64_t(1) << 31) || M >= (int64_t(1) << 31)) return MHC_STATUS_TOO_LARGE;
+    p->M = M;
+    p->n = static_cast<int>(n);
+    p->D = desc->headDim;
+    p->K = K;
+    p->mix = static_cast<int>(mix);
+    p->N = static_cast<int>(2 * mix);
+    p->W = static_cast<int>((mix + 1 + 3) / 4 * 4);
+    p->dtype = desc->dtype;
+    p->hasGamma = desc->hasGamma != 0;
+    p->normEps = desc->normEps;
+    p->hcEps = desc->hcEps;
+    const int64_t sig[4] = {n, desc->headDim, desc->dtype, desc->hasGamma != 0};
+    p->signature = fnv1a(sig, sizeof(sig));
+    return MHC_STATUS_SUCCESS;
+}
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+constexpr int kGroupChunks = 64;      // 4096 K elements per split for large M
+constexpr int64_t kShardRows = 8192;  // from this M up, splits depend on K only
+
+int make_plan(const Problem& p, int smCount, Plan* plan) {
+    Plan pl{};
+    pl.path = 0;
+    pl.tilesM = static_cast<int>((p.M + kRowsPerTile - 1) / kRowsPerTile);
+    pl.chunks = static_cast<int>((p.K + kChunk - 1) / kChunk);
+    // K splits.  From kShardRows rows up, the split count depends on K only (groups
+    // of at most kGroupChunks chunks), so a row's arithmetic, and therefore its
+    // result bits, do not depend on M: token shards of that size reproduce the
+    // unsharded run exactly.  Smaller problems split further to fill the SMs.
+    const int groups = (pl.chunks + kGroupChunks - 1) / kGroupChunks;
+    int splits = groups;
+    if (p.M < kShardRows && pl.tilesM < smCount) splits = std::max(groups, smCount / pl.tilesM);
+    splits = std::min(splits, pl.chunks);
+    pl.splits = splits;
+    const size_t stageBytes = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + static_cast<size_t>(p.N) * kChunk * 2;
+    const size_t smemLimit = 232448;  // sm_100 per-block opt-in maximum
+    const size_t fixed = 1024 /*alignment slack*/ + 256 /*barriers*/;
+    int stages = static_cast<int>((smemLimit - fixed) / stageBytes);
+    stages = std::max(2, std::min(stages, 8));
+    pl.stages = stages;
+    pl.smemBytes = fixed + static_cast<size_t>(stages) * stageBytes;
+    pl.phiOffset = sizeof(WorkspaceHeader);
+    pl.phiBytes = static_cast<size_t>(p.N) * static_cast<size_t>(p.K) * 2;
+    pl.partOffset = align_up(pl.phiOffset + pl.phiBytes, 256);
+    pl.partBytes = static_cast<size_t>(splits) * static_cast<size_t>(p.M) * static_cast<size_t>(p.W) * 4;
+    pl.totalBytes = align_up(pl.partOffset + pl.partBytes, 256);
+    *plan = pl;
+    return MHC_STATUS_SUCCESS;
+}
+
+static int device_sm_count(int* sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return MHC_STATUS_CUDA_ERROR;
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+        return MHC_STATUS_CUDA_ERROR;
+    if (major != 10) return MHC_STATUS_UNSUPPORTED_DEVICE;
+    if (cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return MHC_STATUS_CUDA_ERROR;
+    return MHC_STATUS_SUCCESS;
+}
+
+static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+static bool aligned4(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 3u) == 0; }
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+        return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(fn);
+}
+
+// 2-D K-contiguous matrix [rows][K] of 16-bit elements, 64 x boxRows boxes,
+// 128-byte swizzle (the layout the tensor-core descriptors expect).
+static int encode_2d(EncodeTiledFn enc, CUtensorMap* map, const void* base, int dtype, uint64_t K, uint64_t rows,
+                     uint32_t boxRows) {
+    const cuuint64_t dims[2] = {K, rows};
+    const cuuint64_t strides[1] = {K * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kChunk), boxRows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt =
+        dtype == MHC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
+}
+
+static int prepare_common(const mhcPreDesc_t* desc, Problem* p, Plan* plan, size_t wsBytes, const void* ws) {
+    int rc = make_problem(desc, p);
+    if (rc != 0) return rc;
+    int sms = 0;
+    rc = device_sm_count(&sms);
+    if (rc != 0) return rc;
+    rc = make_plan(*p, sms, plan);
+    if (rc != 0) return rc;
+    if (ws == nullptr) return MHC_STATUS_NULL_POINTER;
+    if (!aligned16(ws)) return MHC_STATUS_MISALIGNED;
+    if (wsBytes < plan->totalBytes) return MHC_STATUS_WORKSPACE_TOO_SMALL;
+    return MHC_STATUS_SUCCESS;
+}
+
+static int run_prepared(const Problem& p, const Plan& plan, const void* x, const float* alpha, const float* bias,
+                        void* hIn, float* hPost, float* hRes, void* workspace, cudaStream_t stream,
+                        cudaEvent_t evBegin = nullptr, cudaEvent_t evEnd = nullptr) {
+    if (x == nullptr || alpha == nullptr || bias == nullptr || hIn == nullptr || hPost == nullptr ||
+        hRes == nullptr)
+        return MHC_STATUS_NULL_POINTER;
+    if (!aligned16(x) || !aligned16(hIn) || !aligned4(hPost) || !aligned4(hRes) || !aligned4(alpha) ||
+        !aligned4(bias))
+        return MHC_STATUS_MISALIGNED;
+    EncodeTiledFn enc = get_encode_fn();
+    if (enc == nullptr) return MHC_STATUS_CUDA_ERROR;
+    CUtensorMap xMap, phiMap;
+    int rc = encode_2d(enc, &xMap, x, p.dtype, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), kRowsPerTile);
+    if (rc != 0) return rc;
+    const void* phiPrep = static_cast<const uint8_t*>(workspace) + plan.phiOffset;
+    rc = encode_2d(enc, &phiMap, phiPrep, p.dtype, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N),
+                   static_cast<uint32_t>(p.N));
+    if (rc != 0) return rc;
+    const int e =
+        launch_run(p, plan, xMap, phiMap, x, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
+    return e == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
+}
+
+}  // namespace mhc
+
+using namespace mhc;
+
+extern "C" {
+
+int mhcPreAbiVersion(void) { return MHC_PRE_ABI_VERSION; }
+
+const char* mhcPreStatusString(int status) {
+    switch (status) {
+        case MHC_STATUS_SUCCESS: return "success";
+        case MHC_STATUS_NULL_POINTER: return "null pointer";
+        case MHC_STATUS_BAD_SHAPE: return "batch, seq and headDim must be positive";
+        case MHC_STATUS_BAD_STREAM_COUNT: return "streams must be 4, 6 or 8";
+        case MHC_STATUS_BAD_HEAD_DIM: return "headDim must be a multiple of 16";
+        case MHC_STATUS_MIX_TOO_LARGE: return "streams*streams + 2*streams exceeds 80";
+        case MHC_STATUS_BAD_DTYPE: return "dtype must be F16 or BF16";
+        case MHC_STATUS_MISALIGNED: return "x, hIn, workspace need 16-byte and fp32 tensors 4-byte alignment";
+        case MHC_STATUS_WORKSPACE_TOO_SMALL: return "workspace smaller than mhcPreGetWorkspaceSize";
+        case MHC_STATUS_CUDA_ERROR: return "CUDA error";
+        case MHC_STATUS_UNSUPPORTED_DEVICE: return "current device is not a B200 (sm_100)";
+        case MHC_STATUS_DEVICE_TIMEOUT: return "a kernel gave up a bounded wait";
+        case MHC_STATUS_NOT_PREPARED: return "workspace holds no prepared weights";
+        case MHC_STATUS_TOO_LARGE: return "problem exceeds a size limit";
+        default: return "unknown status";
+    }
+}
+
+int mhcPreGetWorkspaceSize(const mhcPreDesc_t* desc, size_t* workspaceBytes) {
+    if (workspaceBytes == nullptr) return MHC_STATUS_NULL_POINTER;
+    Problem p;
+    int rc = make_problem(desc, &p);
+    if (rc != 0) return rc;
+    int sms = 0;
+    rc = device_sm_count(&sms);
+    if (rc != 0) return rc;
+    Plan plan;
+    rc = make_plan(p, sms, &plan);
+    if (rc != 0) return rc;
+    *workspaceBytes = plan.totalBytes;
+    return MHC_STATUS_SUCCESS;
+}
+
+int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* out) {
+    if (out == nullptr) return MHC_STATUS_NULL_POINTER;
+    Problem p;
+    int rc = make_problem(desc, &p);
+    if (rc != 0) return rc;
+    int sms = 0;
+    rc = device_sm_count(&sms);
+    if (rc != 0) return rc;
+    Plan plan;
+    rc = make_plan(p, sms, &plan);
+    if (rc != 0) return rc;
+    std::memset(out, 0, sizeof(*out));
+    out->path = plan.path;
+    out->kernelsPerRun = 2;
+    out->gridCtas = plan.tilesM * plan.splits;
+    out->splits = plan.splits;
+    out->rowsPerTile = kRowsPerTile;
+    return MHC_STATUS_SUCCESS;
+}
+
+int mhcPrePrepareWeights(const mhcPreDesc_t* desc, const float* phi, const float* gamma, void* workspace,
+                         size_t workspaceBytes, void* stream) {
+    Problem p;
+    Plan plan;
+    int rc = prepare_common(desc, &p, &plan, workspaceBytes, workspace);
+    if (rc != 0) return rc;
+    if (phi == nullptr || (p.hasGamma && gamma == nullptr)) return MHC_STATUS_NULL_POINTER;
+    if (!aligned4(phi) || (p.hasGamma && !aligned4(gamma))) return MHC_STATUS_MISALIGNED;
+    const int e = launch_prepare(p, plan, phi, gamma, workspace, static_cast<cudaStream_t>(stream));
+    return e == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
+}
+
+int mhcPreRunPrepared(const mhcPreDesc_t* desc, const void* x, const float* alpha, const float* bias, void* hIn,
+                      float* hPost, float* hRes, void* workspace, size_t workspaceBytes, void* stream) {
+    Problem p;
+    Plan plan;
+    int rc = prepare_common(desc, &p, &plan, workspaceBytes, workspace);
+    if (rc != 0) return rc;
+    return run_prepared(p, plan, x, alpha, bias, hIn, hPost, hRes, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int mhcPreRunPreparedProfiled(const mhcPreDesc_t* desc, const void* x, const float* alpha, const float* bias,
+                              void* hIn, float* hPost, float* hRes, void* workspace, size_t workspaceBytes,
+                              void* stream, void* mainKernelBegin, void* mainKernelEnd) {
+    Problem p;
+    Plan plan;
+    int rc = prepare_common(desc, &p, &plan, workspaceBytes, workspace);
+    if (rc != 0) return rc;
+    return run_prepared(p, plan, x, alpha, bias, hIn, hPost, hRes, workspace, static_cast<cudaStream_t>(stream),
+                        static_cast<cudaEvent_t>(mainKernelBegin), static_cast<cudaEvent_t>(mainKernelEnd));
+}
+
+int mhcPreRun(const mhcPreDesc_t* desc, const void* x, const float* phi, const float* alpha, const float* bias,
+              const float* gamma, void* hIn, float* hPost, float* hRes, void* workspace, size_t workspaceBytes,
+              void* stream) {
+    int rc = mhcPrePrepareWeights(desc, phi, gamma, workspace, workspaceBytes, stream);
+    if (rc != 0) return rc;
+    return mhcPreRunPrepared(desc, x, alpha, bias, hIn, hPost, hRes, workspace, workspaceBytes, stream);
+}
+
+int mhcPreGetDeviceStatus(int32_t* deviceStatus) {
+    if (deviceStatus == nullptr) return MHC_STATUS_NULL_POINTER;
+    const int e = read_and_clear_device_status(deviceStatus);
+    return e == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
+}
+
+}  // extern "C"

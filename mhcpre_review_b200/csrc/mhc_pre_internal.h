@@ -1,0 +1,67 @@
+// Internal interface between the C-ABI layer (mhc_pre_api.cpp) and the kernels
+// (mhc_pre_kernels.cu).  Not part of the public ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/mhc_pre.h"
+
+namespace mhc {
+
+// Workspace header written by the weight-preparation kernel.
+struct WorkspaceHeader {
+    uint32_t magic;       // kPreparedMagic once weights are prepared
+    int32_t phiScaleExp;  // fp16: prepared phi' = phi * 2^exp (bf16: 0)
+    uint32_t signature;   // hash of the description the weights were prepared for
+    uint32_t pad[61];     // pad[0]: max |phi'| bits during preparation
+};
+static_assert(sizeof(WorkspaceHeader) == 256, "header is 256 bytes");
+constexpr uint32_t kPreparedMagic = 0x5048434Du;  // "MCHP"
+
+constexpr int kRowsPerTile = 128;  // token rows per tensor-core tile (MMA M)
+constexpr int kChunk = 64;         // K elements per TMA box / pipeline stage (128 bytes)
+constexpr int kMaxMix = 80;
+
+// Everything a launch needs, derived once from the description.
+struct Problem {
+    int64_t M;      // batch * seq
+    int n;          // streams
+    int64_t D;      // head dim
+    int64_t K;      // n * D
+    int mix;        // n*n + 2n
+    int N;          // 2 * mix (hi and lo halves of the prepared weights)
+    int W;          // floats per partial record: mix + 1 rounded up to 4
+    int dtype;      // mhcDtype_t
+    bool hasGamma;
+    float normEps;
+    float hcEps;
+    uint32_t signature;
+};
+
+struct Plan {
+    int path;        // 0: split-K GEMM + epilogue kernels
+    int tilesM;      // ceil(M / 128)
+    int chunks;      // ceil(K / 64)
+    int splits;      // K splits
+    int stages;      // pipeline depth of the GEMM kernel
+    size_t smemBytes;
+    size_t phiOffset, phiBytes;
+    size_t partOffset, partBytes;
+    size_t totalBytes;
+};
+
+int make_problem(const mhcPreDesc_t* desc, Problem* p);
+int make_plan(const Problem& p, int smCount, Plan* plan);
+
+// Kernel launchers (return cudaError_t as int).
+int launch_prepare(const Problem& p, const Plan& plan, const float* phi, const float* gamma, void* workspace,
+                   cudaStream_t stream);
+int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
+               const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
+               void* workspace, cudaStream_t stream, cudaEvent_t evBegin = nullptr, cudaEvent_t evEnd = nullptr);
+int read_and_clear_device_status(int32_t* status);
+
+}  // namespace mhc

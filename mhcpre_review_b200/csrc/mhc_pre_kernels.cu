@@ -1,0 +1,567 @@
+// MhcPre kernels for B200 (sm_100a).
+//
+// Path 0 (every legal shape):
+//   prepare   phi'[j,k] = gamma[k]*phi[j,k] split into hi + lo 16-bit halves of the x
+//             dtype (fp16: scaled by a power of two into the normal range), stored
+//             [2*mix][K] K-contiguous so TMA can stage it for the tensor cores.
+//   gemm      one CTA per (128-row tile, K split): TMA streams 64-wide K chunks of x
+//             and phi' through a shared-memory ring; one thread issues tcgen05.mma
+//             (M=128 token rows, N=2*mix, fp32 accumulators in TMEM); four warps
+//             square-sum the same x chunks from shared memory and add finished
+//             accumulator segments into fp32 registers; the epilogue writes fp32
+//             partial records [split][row][mix partials, sum of squares].
+//   epilogue  one CTA per row: sums the partial records over splits in a fixed
+//             order, computes invRms, hPre/hPost/hRes, then hIn from x.
+//
+// Reference: code/op_kernel/mhc_pre.cpp (the AscendC kernel this replaces).
+#include <algorithm>
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "mhc_pre_internal.h"
+#include "ptx.cuh"
+
+namespace mhc {
+
+__device__ int g_device_status = 0;
+
+__device__ __forceinline__ void set_device_status(int code) { atomicCAS(&g_device_status, 0, code); }
+
+// ---------------------------------------------------------------------------
+// 16-bit helpers
+// ---------------------------------------------------------------------------
+template <int DT>
+__device__ __forceinline__ uint16_t f32_to_x(float v) {
+    if constexpr (DT == MHC_DTYPE_BF16) {
+        return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    } else {
+        return __half_as_ushort(__float2half_rn(v));
+    }
+}
+
+// Unpacks the two 16-bit values of a 32-bit word to fp32 (exact).
+template <int DT>
+__device__ __forceinline__ float2 x2_to_f32(uint32_t w) {
+    if constexpr (DT == MHC_DTYPE_BF16) {
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+    } else {
+        __half2 h = *reinterpret_cast<__half2*>(&w);
+        return __half22float2(h);
+    }
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t f32x2_to_x2(float a, float b) {
+    return static_cast<uint32_t>(f32_to_x<DT>(a)) | (static_cast<uint32_t>(f32_to_x<DT>(b)) << 16);
+}
+
+// ---------------------------------------------------------------------------
+// Weight preparation
+// ---------------------------------------------------------------------------
+__global__ void prep_maxabs_kernel(const float* __restrict__ phi, const float* __restrict__ gamma, int64_t K,
+                                   int mix, uint32_t* __restrict__ maxbits) {
+    const int64_t total = static_cast<int64_t>(mix) * K;
+    float m = 0.0f;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float v = phi[i];
+        if (gamma != nullptr) v = __fmul_rn(v, gamma[i % K]);
+        v = fabsf(v);
+        if (v > m && v <= 3.0e38f) m = v;
+    }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(maxbits, __float_as_uint(m));
+}
+
+template <int DT>
+__global__ void prep_split_kernel(const float* __restrict__ phi, const float* __restrict__ gamma, int64_t K, int mix,
+                                  WorkspaceHeader* __restrict__ hdr, uint16_t* __restrict__ out, uint32_t signature) {
+    int e = 0;
+    if constexpr (DT == MHC_DTYPE_F16) {
+        // Scale so that max|phi'| * 2^e < 2^15: hi and lo then stay normal fp16.
+        const float mx = __uint_as_float(hdr->pad[0]);
+        if (mx > 0.0f) {
+            int ex = 0;
+            frexpf(mx, &ex);
+            e = 15 - ex;
+            e = max(-100, min(100, e));
+        }
+    }
+    const float scale = ldexpf(1.0f, e);
+    const int64_t total = static_cast<int64_t>(mix) * K;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t j = i / K;
+        const int64_t k = i - j * K;
+        float v = phi[i];
+        if (gamma != nullptr) v = __fmul_rn(v, gamma[k]);
+        v = __fmul_rn(v, scale);
+        const uint16_t hb = f32_to_x<DT>(v);
+        float hf;
+        if constexpr (DT == MHC_DTYPE_BF16) {
+            hf = __bfloat162float(__ushort_as_bfloat16(hb));
+        } else {
+            hf = __half2float(__ushort_as_half(hb));
+        }
+        const uint16_t lb = f32_to_x<DT>(__fsub_rn(v, hf));
+        out[j * K + k] = hb;
+        out[(mix + j) * K + k] = lb;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        hdr->phiScaleExp = e;
+        hdr->signature = signature;
+        hdr->magic = kPreparedMagic;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Path 0, kernel 1: split-K GEMM (tcgen05) + square-sum
+// ---------------------------------------------------------------------------
+struct GemmParams {
+    int64_t M;
+    int mix;
+    int W;
+    int chunks;
+    int splits;
+    int stages;
+    float* partials;
+    const WorkspaceHeader* hdr;
+};
+
+template <int N>
+struct GemmCfg {
+    static constexpr int kXBytes = kRowsPerTile * kChunk * 2;  // 16 KB
+    static constexpr int kPhiBytes = N * kChunk * 2;          // N rows x 128 B
+    static constexpr int kStageBytes = kXBytes + kPhiBytes;
+    // two accumulator buffers of N fp32 columns each
+    static constexpr uint32_t kTmemCols = 2 * N <= 64 ? 64 : 2 * N <= 128 ? 128 : 2 * N <= 256 ? 256 : 512;
+    static_assert(N % 16 == 0 && N <= 256, "MMA N for M=128 must be a multiple of 16, at most 256");
+};
+
+constexpr int kGemmThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 square-sum + epilogue
+
+// The tensor core accumulates in fp32 but does not round like an IEEE fp32 adder:
+// over thousands of K steps the accumulator drifts (measured ~1e-4 relative at
+// K = 32768).  Each TMEM accumulation therefore covers only kSegChunks 64-wide
+// K chunks; finished segments are added into IEEE fp32 registers by the epilogue
+// warps while the MMA fills the other accumulator buffer.
+constexpr int kSegChunks = 4;
+
+template <int DT, int N>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_sumsq_kernel(const __grid_constant__ CUtensorMap xMap, const __grid_constant__ CUtensorMap phiMap,
+                      const GemmParams p) {
+    using Cfg = GemmCfg<N>;
+    constexpr int MIX = N / 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int S = p.stages;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * Cfg::kStageBytes);
+    uint64_t* empty = full + S;
+    uint64_t* accFull = empty + S;     // [2]
+    uint64_t* accEmpty = accFull + 2;  // [2]
+    uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(accEmpty + 2);
+    volatile int* abortFlag = reinterpret_cast<volatile int*>(tmemSlot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tile = blockIdx.x;
+    const int split = blockIdx.y;
+    const int cBegin = static_cast<int>((static_cast<int64_t>(split) * p.chunks) / p.splits);
+    const int cEnd = static_cast<int>((static_cast<int64_t>(split + 1) * p.chunks) / p.splits);
+    const int nChunks = cEnd - cBegin;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1 + 4);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accFull[b], 1);
+            mbar_init(&accEmpty[b], 4);
+        }
+        *abortFlag = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmemSlot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&xMap);
+        tma_prefetch_desc(&phiMap);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tacc = *tmemSlot;
+    const bool prepared = p.hdr->magic == kPreparedMagic;
+    if (!prepared && threadIdx.x == 0) set_device_status(MHC_STATUS_NOT_PREPARED);
+
+    auto stage_x = [&](int s) { return smem + static_cast<size_t>(s) * Cfg::kStageBytes; };
+    auto stage_phi = [&](int s) { return smem + static_cast<size_t>(s) * Cfg::kStageBytes + Cfg::kXBytes; };
+    auto fail = [&]() {
+        set_device_status(MHC_STATUS_DEVICE_TIMEOUT);
+        *abortFlag = 1;
+    };
+
+    if (prepared && nChunks > 0) {
+        if (warp == 0) {
+            if (lane == 0) {
+                int issued = 0;
+                for (int i = 0; i < nChunks; ++i) {
+                    const int s = i % S;
+                    const uint32_t use = static_cast<uint32_t>(i / S);
+                    if (i >= S && !mbar_wait(&empty[s], (use & 1u) ^ 1u, abortFlag)) {
+                        fail();
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+                    const int kc = (cBegin + i) * kChunk;
+                    tma_load_2d(stage_x(s), &xMap, &full[s], kc, tile * kRowsPerTile);
+                    tma_load_2d(stage_phi(s), &phiMap, &full[s], kc, 0);
+                    issued = i + 1;
+                }
+                if (*abortFlag != 0) {
+                    // Let copies already in flight land before the CTA exits (bounded).
+                    for (int i = (issued > S ? issued - S : 0); i < issued; ++i) {
+                        mbar_wait(&full[i % S], static_cast<uint32_t>(i / S) & 1u, nullptr, 100000000ull);
+                    }
+                }
+            }
+        } else if (warp == 1) {
+            if (lane == 0) {
+                constexpr uint32_t idesc = idesc_f16(DT, kRowsPerTile, N);
+                for (int i = 0; i < nChunks; ++i) {
+                    const int s = i % S;
+                    const int seg = i / kSegChunks;
+                    const int b = seg & 1;
+                    if (i % kSegChunks == 0 && seg >= 2 &&
+                        !mbar_wait(&accEmpty[b], static_cast<uint32_t>((seg >> 1) - 1) & 1u, abortFlag)) {
+                        fail();
+                        break;
+                    }
+                    if (!mbar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u, abortFlag)) {
+                        fail();
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(stage_x(s));
+                    const uint32_t b0 = smem_u32(stage_phi(s));
+                    const uint32_t d = tacc + static_cast<uint32_t>(b * N);
+#pragma unroll
+                    for (int k16 = 0; k16 < kChunk / 16; ++k16) {
+                        mma_f16_ss(d, sdesc_sw128(a0 + k16 * 32), sdesc_sw128(b0 + k16 * 32), idesc,
+                                   (i % kSegChunks != 0 || k16 > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&empty[s]);
+                    if (i % kSegChunks == kSegChunks - 1 || i == nChunks - 1) mma_commit(&accFull[b]);
+                }
+            }
+        } else {
+            // warps 2..5: one token row per thread; TMEM lane quadrant = warp % 4
+            const int q = warp & 3;
+            const int row = q * 32 + lane;
+            const uint32_t lane_base = tacc + (static_cast<uint32_t>(q * 32) << 16);
+            float run[MIX];
+#pragma unroll
+            for (int j = 0; j < MIX; ++j) run[j] = 0.0f;
+            bool ok = true;
+            // Adds finished accumulator segment `seg` into run[] and frees its buffer.
+            auto flush = [&](int seg) -> bool {
+                const int b = seg & 1;
+                // warp-uniform outcome: the TMEM loads below are warp-collective
+                if (!__all_sync(0xffffffffu, mbar_wait(&accFull[b], static_cast<uint32_t>(seg >> 1) & 1u, abortFlag)))
+                    return false;
+                tc_fence_after();
+#pragma unroll
+                for (int j0 = 0; j0 < MIX; j0 += 8) {
+                    uint32_t hi[8], lo[8];
+                    tmem_ld_x8(lane_base + b * N + j0, hi);
+                    tmem_ld_x8(lane_base + b * N + MIX + j0, lo);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) {
+                        run[j0 + t] =
+                            __fadd_rn(run[j0 + t], __fadd_rn(__uint_as_float(hi[t]), __uint_as_float(lo[t])));
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&accEmpty[b]);
+                return true;
+            };
+            float ss = 0.0f;
+            for (int i = 0; i < nChunks; ++i) {
+                const int s = i % S;
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u, abortFlag))) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t base = smem_u32(stage_x(s)) + row * 128;
+                float part = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint4 v = lds128(base + ((j ^ (row & 7)) << 4));
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const float2 f = x2_to_f32<DT>(w[t]);
+                        part = fmaf(f.x, f.x, part);
+                        part = fmaf(f.y, f.y, part);
+                    }
+                }
+                ss += part;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+                const int seg = i / kSegChunks;
+                if ((i % kSegChunks == kSegChunks - 1 || i == nChunks - 1) && seg >= 1) {
+                    if (!flush(seg - 1)) {
+                        ok = false;
+                        break;
+                    }
+                }
+            }
+            ok = __all_sync(0xffffffffu, ok);
+            if (ok) ok = __all_sync(0xffffffffu, flush((nChunks - 1) / kSegChunks));
+            if (ok) {
+                const float unscale = ldexpf(1.0f, -p.hdr->phiScaleExp);
+                const int64_t grow = static_cast<int64_t>(tile) * kRowsPerTile + row;
+                if (grow < p.M) {
+                    float* out = p.partials + (static_cast<int64_t>(split) * p.M + grow) * p.W;
+#pragma unroll
+                    for (int j0 = 0; j0 < MIX; j0 += 4) {
+                        float4 a;
+                        a.x = __fmul_rn(run[j0 + 0], unscale);
+                        a.y = __fmul_rn(run[j0 + 1], unscale);
+                        a.z = __fmul_rn(run[j0 + 2], unscale);
+                        a.w = __fmul_rn(run[j0 + 3], unscale);
+                        *reinterpret_cast<float4*>(out + j0) = a;
+                    }
+                    out[MIX] = ss;
+                }
+            } else if (lane == 0) {
+                fail();
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tacc, Cfg::kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Path 0, kernel 2: split reduction, epilogue, hIn
+// ---------------------------------------------------------------------------
+struct EpiParams {
+    int64_t M;
+    int64_t D;
+    int64_t K;
+    int mix;
+    int W;
+    int splits;
+    float invK;
+    float normEps;
+    float hcEps;
+    const float* partials;
+    const uint16_t* x;
+    const float* alpha;
+    const float* bias;
+    uint16_t* hIn;
+    float* hPost;
+    float* hRes;
+};
+
+constexpr int kEpiThreads = 128;
+
+// sigmoid(v) = 1 / (1 + exp(-v)), in the operation order of the reference's
+// Sigmoid helper (code/op_kernel/mhc_pre.cpp:542-555).
+__device__ __forceinline__ float sigmoid_ref(float v) {
+    float t = __fmul_rn(v, -1.0f);
+    t = expf(t);
+    t = __fadd_rn(t, 1.0f);
+    return __fdiv_rn(1.0f, t);
+}
+
+template <int DT, int NS>
+__global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiParams p) {
+    constexpr int mix = NS * NS + 2 * NS;
+    __shared__ float sMix[mix];
+    __shared__ float sPre[NS];
+    __shared__ float sSum;
+    const int64_t r = blockIdx.x;
+    const int tid = threadIdx.x;
+    if (tid <= mix) {
+        float acc = 0.0f;
+        for (int sp = 0; sp < p.splits; ++sp) {
+            acc = __fadd_rn(acc, p.partials[(static_cast<int64_t>(sp) * p.M + r) * p.W + tid]);
+        }
+        if (tid < mix) sMix[tid] = acc; else sSum = acc;
+    }
+    __syncthreads();
+    // invRms = 1 / Sqrt(sum * invFlatDim + normEps)   (mhc_pre.cpp:504-519)
+    float v = __fmul_rn(sSum, p.invK);
+    v = __fadd_rn(v, p.normEps);
+    const float invRms = __fdiv_rn(1.0f, __fsqrt_rn(v));
+    const float a0 = __ldg(p.alpha + 0), a1 = __ldg(p.alpha + 1), a2 = __ldg(p.alpha + 2);
+    if (tid < NS) {
+        const float sPreScale = __fmul_rn(invRms, a0);
+        const float sPostScale = __fmul_rn(invRms, a1);
+        float t = __fadd_rn(__fmul_rn(sMix[tid], sPreScale), __ldg(p.bias + tid));
+        sPre[tid] = __fadd_rn(sigmoid_ref(t), p.hcEps);
+        float u = __fadd_rn(__fmul_rn(sMix[NS + tid], sPostScale), __ldg(p.bias + NS + tid));
+        p.hPost[r * NS + tid] = __fmul_rn(sigmoid_ref(u), 2.0f);
+    }
+    if (tid < NS * NS) {
+        const float sResScale = __fmul_rn(invRms, a2);
+        p.hRes[r * NS * NS + tid] =
+            __fadd_rn(__fmul_rn(sMix[2 * NS + tid], sResScale), __ldg(p.bias + 2 * NS + tid));
+    }
+    __syncthreads();
+    float pre[NS];
+#pragma unroll
+    for (int s = 0; s < NS; ++s) pre[s] = sPre[s];
+    const uint4* xr = reinterpret_cast<const uint4*>(p.x + r * p.K);
+    uint4* hr = reinterpret_cast<uint4*>(p.hIn + r * p.D);
+    const int64_t vecPerStream = p.D / 8;
+    for (int64_t vi = tid; vi < vecPerStream; vi += kEpiThreads) {
+        float acc[8];
+        {
+            const uint4 w = __ldg(xr + vi);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float2 f = x2_to_f32<DT>(ws[t]);
+                acc[2 * t] = __fmul_rn(f.x, pre[0]);
+                acc[2 * t + 1] = __fmul_rn(f.y, pre[0]);
+            }
+        }
+#pragma unroll
+        for (int s = 1; s < NS; ++s) {
+            const uint4 w = __ldg(xr + s * vecPerStream + vi);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float2 f = x2_to_f32<DT>(ws[t]);
+                acc[2 * t] = __fadd_rn(acc[2 * t], __fmul_rn(f.x, pre[s]));
+                acc[2 * t + 1] = __fadd_rn(acc[2 * t + 1], __fmul_rn(f.y, pre[s]));
+            }
+        }
+        uint4 o;
+        o.x = f32x2_to_x2<DT>(acc[0], acc[1]);
+        o.y = f32x2_to_x2<DT>(acc[2], acc[3]);
+        o.z = f32x2_to_x2<DT>(acc[4], acc[5]);
+        o.w = f32x2_to_x2<DT>(acc[6], acc[7]);
+        hr[vi] = o;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+int launch_prepare(const Problem& p, const Plan& plan, const float* phi, const float* gamma, void* workspace,
+                   cudaStream_t stream) {
+    auto* hdr = reinterpret_cast<WorkspaceHeader*>(workspace);
+    auto* out = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + plan.phiOffset);
+    cudaError_t e = cudaMemsetAsync(hdr, 0, sizeof(WorkspaceHeader), stream);
+    if (e != cudaSuccess) return e;
+    const float* g = p.hasGamma ? gamma : nullptr;
+    const int64_t total = static_cast<int64_t>(p.mix) * p.K;
+    const int threads = 256;
+    const int blocks = static_cast<int>(std::min<int64_t>((total + threads - 1) / threads, 148 * 8));
+    if (p.dtype == MHC_DTYPE_F16) {
+        prep_maxabs_kernel<<<blocks, threads, 0, stream>>>(phi, g, p.K, p.mix, &hdr->pad[0]);
+        prep_split_kernel<MHC_DTYPE_F16><<<blocks, threads, 0, stream>>>(phi, g, p.K, p.mix, hdr, out, p.signature);
+    } else {
+        prep_split_kernel<MHC_DTYPE_BF16><<<blocks, threads, 0, stream>>>(phi, g, p.K, p.mix, hdr, out, p.signature);
+    }
+    return cudaGetLastError();
+}
+
+template <int DT, int N>
+static int launch_gemm(const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap, const GemmParams& gp,
+                       cudaStream_t stream) {
+    auto kern = gemm_sumsq_kernel<DT, N>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(plan.smemBytes));
+    if (e != cudaSuccess) return e;
+    dim3 grid(plan.tilesM, plan.splits);
+    kern<<<grid, kGemmThreads, plan.smemBytes, stream>>>(xMap, phiMap, gp);
+    return cudaGetLastError();
+}
+
+template <int DT, int NS>
+static int launch_epi(const Problem& p, const EpiParams& ep, cudaStream_t stream) {
+    epilogue_hin_kernel<DT, NS><<<static_cast<unsigned>(p.M), kEpiThreads, 0, stream>>>(ep);
+    return cudaGetLastError();
+}
+
+int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
+               const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
+               void* workspace, cudaStream_t stream, cudaEvent_t evBegin, cudaEvent_t evEnd) {
+    GemmParams gp;
+    gp.M = p.M;
+    gp.mix = p.mix;
+    gp.W = p.W;
+    gp.chunks = plan.chunks;
+    gp.splits = plan.splits;
+    gp.stages = plan.stages;
+    gp.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.partOffset);
+    gp.hdr = reinterpret_cast<const WorkspaceHeader*>(workspace);
+    int rc;
+    const bool bf = p.dtype == MHC_DTYPE_BF16;
+    if (evBegin != nullptr && cudaEventRecord(evBegin, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    switch (p.n) {
+        case 4: rc = bf ? launch_gemm<MHC_DTYPE_BF16, 48>(plan, xMap, phiMap, gp, stream)
+                        : launch_gemm<MHC_DTYPE_F16, 48>(plan, xMap, phiMap, gp, stream); break;
+        case 6: rc = bf ? launch_gemm<MHC_DTYPE_BF16, 96>(plan, xMap, phiMap, gp, stream)
+                        : launch_gemm<MHC_DTYPE_F16, 96>(plan, xMap, phiMap, gp, stream); break;
+        default: rc = bf ? launch_gemm<MHC_DTYPE_BF16, 160>(plan, xMap, phiMap, gp, stream)
+                         : launch_gemm<MHC_DTYPE_F16, 160>(plan, xMap, phiMap, gp, stream); break;
+    }
+    if (rc != 0) return rc;
+    if (evEnd != nullptr && cudaEventRecord(evEnd, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    EpiParams ep;
+    ep.M = p.M;
+    ep.D = p.D;
+    ep.K = p.K;
+    ep.mix = p.mix;
+    ep.W = p.W;
+    ep.splits = plan.splits;
+    ep.invK = 1.0f / static_cast<float>(p.K);
+    ep.normEps = p.normEps;
+    ep.hcEps = p.hcEps;
+    ep.partials = gp.partials;
+    ep.x = static_cast<const uint16_t*>(x);
+    ep.alpha = alpha;
+    ep.bias = bias;
+    ep.hIn = static_cast<uint16_t*>(hIn);
+    ep.hPost = hPost;
+    ep.hRes = hRes;
+    switch (p.n) {
+        case 4: return bf ? launch_epi<MHC_DTYPE_BF16, 4>(p, ep, stream) : launch_epi<MHC_DTYPE_F16, 4>(p, ep, stream);
+        case 6: return bf ? launch_epi<MHC_DTYPE_BF16, 6>(p, ep, stream) : launch_epi<MHC_DTYPE_F16, 6>(p, ep, stream);
+        default: return bf ? launch_epi<MHC_DTYPE_BF16, 8>(p, ep, stream) : launch_epi<MHC_DTYPE_F16, 8>(p, ep, stream);
+    }
+}
+
+int read_and_clear_device_status(int32_t* status) {
+    int v = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int));
+    if (e != cudaSuccess) return e;
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return e;
+    *status = v;
+    return 0;
+}
+
+}  // namespace mhc
