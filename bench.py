@@ -1,0 +1,410 @@
+"""MhcPre benchmark on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c4]
+
+A step is one MhcPre call over one batch of the workload (default: BASELINE
+config 4, M = 65536 tokens (B=16, S=4096), n=4, D=7168, bf16, gamma on) with the
+weights prepared once beforehand (they are model parameters).  Each GPU processes
+its own batch of that size (token sharding, phi replicated, no collective on the
+data path), so scaling is weak; value = tokens all ranks processed / the slowest
+rank's device time.  Inputs (3.76 GB of x per GPU) are larger than the 126 MB L2,
+so no flush is needed between steps.
+
+The JSON line also carries:
+  roofline      the main kernel's algorithmic bytes per launch / its average launch
+                time (CUDA events recorded around that kernel inside the timed loop),
+                against the measured HBM copy bandwidth in MEASURED_PEAKS.json;
+                traffic = DRAM bytes per launch from the committed ncu summary.
+  cpu_baseline  the CPU oracle (a port of the reference's formula) timed on this
+                box's host cores on a bounded sample (rank 0, N=1).
+  e2e           the same metric through the public API with host buffers: per step,
+                pinned host x is copied in, the operator runs, hIn/hPost/hRes are
+                copied out (chunked over three streams so copies overlap compute).
+  clocks        nvidia-smi samples taken during the timed region.
+--impl reference times the reference's own CPU formula (the oracle port; the
+reference itself is AscendC for Ascend 910B and cannot run here) on all host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MhcPre tokens/s & HBM GB/s (% of 8 TB/s), n=4 D=7168 bf16, at 1/2/4/8 B200"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c4")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=0, help="override the config's batch (profiling cases)")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic(kernel: str, workload: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(kernel, {}).get(workload)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = None
+
+    def __enter__(self):
+        try:
+            self.out = open(f"/tmp/mhc_clocks_{os.getpid()}.csv", "w+")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.out is None:
+            return None
+        self.out.flush()
+        self.out.seek(0)
+        rows = [[c.strip() for c in r.split(",")] for r in self.out.read().strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def time_oracle(cfg, x_bits, phi, alpha, bias, gamma, rows, threads):
+    from oracle import ref
+    t0 = time.perf_counter()
+    ref.mhc_pre_ref(x_bits[:rows], phi, alpha, bias, gamma, cfg.n, cfg.D, cfg.dtype, threads=threads)
+    return time.perf_counter() - t0
+
+
+def host_inputs(cfg):
+    """Inputs of the workload on the host (for the CPU runs), generated exactly like
+    the GPU run's (same seeds) when a GPU is present, else with numpy."""
+    import numpy as np
+    try:
+        import torch
+        if torch.cuda.is_available():
+            from mhcpre_review_b200.configs import make_inputs
+            inp = make_inputs(cfg)
+            xb = inp["x"].reshape(cfg.M, cfg.K).view(torch.int16).cpu().numpy().view(np.uint16)
+            g = None if inp["gamma"] is None else inp["gamma"].reshape(-1).cpu().numpy()
+            out = (xb, inp["phi"].cpu().numpy(), inp["alpha"].cpu().numpy(), inp["bias"].cpu().numpy(), g)
+            del inp
+            torch.cuda.empty_cache()
+            return out
+    except Exception:
+        pass
+    from oracle import ref
+    rng = np.random.default_rng(cfg.seed)
+    rows = min(cfg.M, 16384)
+    x = ref.from_float(rng.standard_normal((rows, cfg.K), dtype=np.float32), cfg.dtype)
+    phi = (rng.standard_normal((cfg.mix, cfg.K)) * cfg.phi_std).astype(np.float32)
+    g = (1 + 0.05 * rng.standard_normal(cfg.K)).astype(np.float32) if cfg.gamma else None
+    alpha = (0.5 + rng.random(3)).astype(np.float32)
+    bias = (0.1 * rng.standard_normal(cfg.mix)).astype(np.float32)
+    return x, phi, alpha, bias, g
+
+
+def cpu_sample_rows(cfg, x, phi, alpha, bias, gamma, threads, target_s=10.0):
+    """Rows for a bounded CPU sample of about target_s seconds."""
+    probe = min(len(x), 512)
+    t = time_oracle(cfg, x, phi, alpha, bias, gamma, probe, threads)
+    per_row = max(t / probe, 1e-7)
+    return int(max(probe, min(len(x), target_s / per_row)))
+
+
+def workload_config(cfg, n_gpus):
+    return {"workload": f"{cfg.name}: M={cfg.M} (B={cfg.batch},S={cfg.seq}) per GPU, n={cfg.n}, D={cfg.D}, "
+                        f"{cfg.dtype}, gamma {'on' if cfg.gamma else 'off'}",
+            "tokens_per_gpu": cfg.M, "global_tokens": cfg.M * n_gpus, "streams": cfg.n, "head_dim": cfg.D,
+            "parallelism": f"token-sharded x{n_gpus}, phi replicated, no collective",
+            "l2": "inputs larger than L2 (x = %.2f GB per GPU), no flush" % (cfg.M * cfg.K * 2 / 1e9)}
+
+
+def run_reference(args, cfg, world, rank):
+    """CPU reference arm: the reference formula (oracle port) on all host cores."""
+    if rank != 0:
+        return
+    x, phi, alpha, bias, gamma = host_inputs(cfg)
+    threads = cpu_cores()
+    rows = cpu_sample_rows(cfg, x, phi, alpha, bias, gamma, threads, target_s=8.0)
+    for _ in range(args.warmup):
+        time_oracle(cfg, x, phi, alpha, bias, gamma, min(rows, 256), threads)
+    times = [time_oracle(cfg, x, phi, alpha, bias, gamma, rows, threads) for _ in range(args.steps)]
+    per_step = sum(times) / len(times)
+    value = rows / per_step
+    sample = f"{rows} of the {cfg.M} rows of {cfg.name} per step (the same rows every step)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3 * cfg.M / rows,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": cfg.dtype,
+        "data": "synthetic (seeded, BASELINE config shapes and distributions)",
+        "config": workload_config(cfg, args.gpus),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference operator is AscendC for Ascend 910B; its own CPU formula "
+                "(cloud_runner/runner.cpp:122-192, audit_group_vec.py:279-324) is timed via the oracle port",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def measure_e2e(mp, inp, cfg, steps, pg, dist, world):
+    """Public API with pinned host buffers: H2D x, run, D2H outputs, per step,
+    chunked over rows on three streams so the copies overlap the kernels."""
+    import torch
+    x = inp["x"]
+    chunks = 8 if cfg.M % 8 == 0 and cfg.M // 8 >= 8192 else 1
+    rows = cfg.M // chunks
+    xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+    xh.copy_(x)
+    hin_h = torch.empty((cfg.batch, cfg.seq, cfg.D), dtype=x.dtype, pin_memory=True)
+    post_h = torch.empty((cfg.batch, cfg.seq, cfg.n), dtype=torch.float32, pin_memory=True)
+    res_h = torch.empty((cfg.batch, cfg.seq, cfg.n, cfg.n), dtype=torch.float32, pin_memory=True)
+    cex = mp.MhcPre(1, rows, cfg.n, cfg.D, x.dtype, cfg.gamma, cfg.norm_eps, cfg.hc_eps)
+    cex.prepare(inp["phi"], inp["gamma"])
+    xd = torch.empty((2, rows, cfg.n, cfg.D), dtype=x.dtype, device="cuda")
+    od = [cex.outputs(x.dtype) for _ in range(2)]
+    s_in, s_run, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    xh_r = xh.reshape(cfg.M, cfg.n, cfg.D)
+    hin_r, post_r, res_r = hin_h.reshape(cfg.M, cfg.D), post_h.reshape(cfg.M, cfg.n), res_h.reshape(cfg.M, cfg.n, cfg.n)
+    h2d = cfg.M * cfg.K * 2
+    d2h = cfg.M * cfg.D * 2 + cfg.M * cfg.n * 4 + cfg.M * cfg.n * cfg.n * 4
+
+    def one_step():
+        done_out = [None, None]
+        for c in range(chunks):
+            b = c % 2
+            with torch.cuda.stream(s_in):
+                if done_out[b] is not None:
+                    s_in.wait_event(done_out[b])
+                xd[b].copy_(xh_r[c * rows:(c + 1) * rows], non_blocking=True)
+                ev_in = torch.cuda.Event()
+                ev_in.record(s_in)
+            with torch.cuda.stream(s_run):
+                s_run.wait_event(ev_in)
+                cex(xd[b].reshape(1, rows, cfg.n, cfg.D), inp["alpha"], inp["bias"], out=od[b], stream=s_run)
+                ev_run = torch.cuda.Event()
+                ev_run.record(s_run)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_run)
+                hin_r[c * rows:(c + 1) * rows].copy_(od[b][0].reshape(rows, cfg.D), non_blocking=True)
+                post_r[c * rows:(c + 1) * rows].copy_(od[b][1].reshape(rows, cfg.n), non_blocking=True)
+                res_r[c * rows:(c + 1) * rows].copy_(od[b][2].reshape(rows, cfg.n, cfg.n), non_blocking=True)
+                ev_o = torch.cuda.Event()
+                ev_o.record(s_out)
+                done_out[b] = ev_o
+        torch.cuda.current_stream().wait_stream(s_out)
+
+    one_step()
+    torch.cuda.synchronize()
+    if pg:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(steps):
+        one_step()
+    t1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([t0.elapsed_time(t1) / steps], device="cuda", dtype=torch.float64)
+    if pg:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"value": world * cfg.M / (ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": ms, "chunks": chunks, "pinned_host": True}
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_env()
+    from mhcpre_review_b200.configs import CONFIGS, with_shape as _ws
+    cfg = CONFIGS[args.config]
+    if args.batch > 0:
+        cfg = _ws(cfg, batch=args.batch, name=f"{cfg.name}_b{args.batch}")
+    if world > 1:
+        args.gpus = world
+
+    if args.impl == "reference":
+        run_reference(args, cfg, world, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    pg = False
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        pg = True
+
+    import mhcpre_review_b200 as mp
+    from mhcpre_review_b200.configs import make_inputs, with_shape
+
+    # each rank: its own batch (x seed offset by rank), weights identical on all ranks
+    inp = make_inputs(with_shape(cfg, seed=cfg.seed + 1000 * rank) if rank else cfg)
+    if rank:
+        w = make_inputs(with_shape(cfg, batch=1, seq=1))  # same weight seeds as rank 0
+        inp.update(phi=w["phi"], gamma=w["gamma"], alpha=w["alpha"], bias=w["bias"])
+    x = inp["x"]
+    ex = mp.MhcPre(cfg.batch, cfg.seq, cfg.n, cfg.D, x.dtype, cfg.gamma, cfg.norm_eps, cfg.hc_eps)
+    ex.prepare(inp["phi"], inp["gamma"])
+    out = ex.outputs(x.dtype)
+    plan = ex.plan
+
+    for _ in range(max(args.warmup, 3)):
+        ex(x, inp["alpha"], inp["bias"], out=out)
+    torch.cuda.synchronize()
+    if pg:
+        dist.barrier()
+
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for e in ev_b + ev_e:
+        e.record()  # materialise the CUDA events before handing them to the library
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        if pg:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t_start.record()
+        for i in range(args.steps):
+            ex.run_profiled(x, inp["alpha"], inp["bias"], out, ev_b[i], ev_e[i])
+        t_end.record()
+        torch.cuda.synchronize()
+        if pg:
+            dist.barrier()
+    ms_total = t_start.elapsed_time(t_end)
+    main_ms = [b.elapsed_time(e) for b, e in zip(ev_b, ev_e)]
+    status = mp.device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status}")
+
+    t = torch.tensor([ms_total], device="cuda", dtype=torch.float64)
+    if pg:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item()) / args.steps
+    value = world * cfg.M / (ms_step * 1e-3)
+
+    # roofline of the main kernel
+    peak, peak_kind = measured_peaks()
+    main_avg_ms = sum(main_ms) / len(main_ms)
+    if plan["path"] == 1:
+        kernel, kbytes = "mhc_pre_fused", cfg.algorithmic_bytes()
+    else:
+        kernel = "gemm_sumsq"
+        kbytes = cfg.M * cfg.K * 2 + 4 * cfg.K * cfg.mix + (4 * cfg.K if cfg.gamma else 0)
+    achieved = kbytes / (main_avg_ms * 1e-3) / 1e9
+    op_gbs = cfg.algorithmic_bytes() / (ms_step * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "traffic": committed_traffic(kernel, cfg.name), "algorithmic_bytes_per_launch": kbytes,
+                "launch_ms": main_avg_ms, "op_GBps": op_gbs, "op_frac_of_8TBps": op_gbs / 8000.0}
+
+    e2e = None
+    if not args.no_e2e:
+        del out
+        torch.cuda.empty_cache()
+        e2e = measure_e2e(mp, inp, cfg, args.e2e_steps, pg, dist, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        xb, phi, alpha, bias, gamma = host_inputs(cfg)
+        threads = cpu_cores()
+        rows = cpu_sample_rows(cfg, xb, phi, alpha, bias, gamma, threads, target_s=10.0)
+        secs = time_oracle(cfg, xb, phi, alpha, bias, gamma, rows, threads)
+        cpu = {"value": rows / secs, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"first {rows} of the {cfg.M} rows of {cfg.name} (same inputs), one pass, {secs:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": cfg.dtype,
+            "data": "synthetic (seeded, BASELINE config shapes and distributions)",
+            "config": workload_config(cfg, world), "plan": plan, "gpu_launches": args.steps * plan["kernels_per_run"],
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if pg:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
