@@ -83,7 +83,8 @@ def committed_traffic(kernel: str, workload: str):
 
 
 class ClockSampler:
-    """Samples nvidia-smi every 200 ms during the timed region."""
+    """Samples nvidia-smi every 20 ms during the timed region (the first sample is
+    taken before the region starts)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -98,8 +99,12 @@ class ClockSampler:
         try:
             self.out = open(f"/tmp/mhc_clocks_{os.getpid()}.csv", "w+")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.out,
+                                          "--format=csv,noheader,nounits", "-lms", "20"], stdout=self.out,
                                          stderr=subprocess.DEVNULL)
+            # wait (bounded) for the first sample so the timed region is covered
+            t0 = time.time()
+            while time.time() - t0 < 5.0 and os.path.getsize(self.out.name) == 0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
         return self
