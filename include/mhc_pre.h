@@ -127,6 +127,32 @@ MHC_API int mhcPreRunPreparedProfiled(const mhcPreDesc_t* desc, const void* x, c
                                       void* hIn, float* hPost, float* hRes, void* workspace, size_t workspaceBytes,
                                       void* stream, void* mainKernelBegin, void* mainKernelEnd);
 
+/* Size of the library's fixed device scratch area used by mhcPreRunNoAlloc. */
+#define MHC_PRE_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+
+/* mhcPreRun for callers that cannot allocate device memory while they run: a
+ * plugin handed only its tensors' device pointers and no allocator, a serving
+ * runtime whose device memory is planned and locked before traffic starts, or a
+ * latency-critical loop that must not call cudaMalloc (it can synchronize the
+ * device).  Same inputs, outputs and results as mhcPreRun, but no workspace
+ * argument: the prepared weights and the split-K partial records live in one
+ * 64 MiB array (MHC_PRE_NOALLOC_SCRATCH_BYTES) compiled into the library, which
+ * every GPU that loads the library keeps until the process exits.  A problem
+ * whose mhcPreGetWorkspaceSize exceeds that size is rejected with
+ * MHC_STATUS_TOO_LARGE before anything runs (config 4, M = 65536, n = 4,
+ * D = 7168, needs 54 MB and fits).  The call itself allocates nothing: no
+ * cudaMalloc, no cudaFree, no allocating library routine.  The first call on a
+ * device looks up that device's copy of the array (cudaGetSymbolAddress, which
+ * may load the library's device code); make that first call before any stream
+ * capture.  All calls on a device share the one array and it keeps the last
+ * call's contents, so calls that can overlap on the GPU (different streams or
+ * host threads without ordering between them) race and corrupt each other:
+ * issue them in order, for example on one stream.  No counterpart in the
+ * reference. */
+MHC_API int mhcPreRunNoAlloc(const mhcPreDesc_t* desc, const void* x, const float* phi, const float* alpha,
+                             const float* bias, const float* gamma, void* hIn, float* hPost, float* hRes,
+                             void* stream);
+
 /* Execution plan chosen for a description on the current device (for tests,
  * benchmarks and profiling; no reference counterpart). */
 typedef struct {

@@ -34,7 +34,7 @@ STATUS_NAMES = {
 EXPORTED_SYMBOLS = (
     "mhcPreGetWorkspaceSize", "mhcPrePrepareWeights", "mhcPreRun", "mhcPreRunPrepared",
     "mhcPreRunPreparedProfiled", "mhcPreQueryPlan", "mhcPreGetDeviceStatus", "mhcPreStatusString",
-    "mhcPreAbiVersion",
+    "mhcPreAbiVersion", "mhcPreRunNoAlloc",
 )
 
 
@@ -80,6 +80,7 @@ def lib():
         L.mhcPreRunPrepared.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp, sz, vp]
         L.mhcPreRunPreparedProfiled.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp, sz, vp, vp, vp]
         L.mhcPreQueryPlan.argtypes = [dp, ctypes.POINTER(MhcPrePlan)]
+        L.mhcPreRunNoAlloc.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
         L.mhcPreGetDeviceStatus.argtypes = [ctypes.POINTER(ctypes.c_int32)]
         L.mhcPreStatusString.argtypes = [ctypes.c_int]
         L.mhcPreStatusString.restype = ctypes.c_char_p

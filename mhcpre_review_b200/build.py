@@ -16,7 +16,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libmhcpre_b200.so"
-SOURCES = ["mhc_pre_kernels.cu", "mhc_pre_api.cpp"]
+SOURCES = ["mhc_pre_kernels.cu", "mhc_pre_api.cpp", "mhc_pre_noalloc.cu"]
 HEADERS = ["ptx.cuh", "mhc_pre_internal.h"]
 
 NVCC_FLAGS = [

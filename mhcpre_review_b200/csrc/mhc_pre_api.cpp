@@ -168,6 +168,27 @@ static int run_prepared(const Problem& p, const Plan& plan, const void* x, const
     return e == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
 }
 
+// Helpers for the no-allocation entry point (mhc_pre_noalloc.cu): the same
+// validation, plan, weight preparation and launch as the entry points below,
+// with the workspace supplied by the caller of these helpers.
+int plan_for(const mhcPreDesc_t* desc, Problem* p, Plan* plan) {
+    int rc = make_problem(desc, p);
+    if (rc != 0) return rc;
+    int sms = 0;
+    rc = device_sm_count(&sms);
+    if (rc != 0) return rc;
+    return make_plan(*p, sms, plan);
+}
+
+int prepare_and_run(const Problem& p, const Plan& plan, const void* x, const float* phi, const float* alpha,
+                    const float* bias, const float* gamma, void* hIn, float* hPost, float* hRes, void* workspace,
+                    cudaStream_t stream) {
+    if (phi == nullptr || (p.hasGamma && gamma == nullptr)) return MHC_STATUS_NULL_POINTER;
+    if (!aligned4(phi) || (p.hasGamma && !aligned4(gamma))) return MHC_STATUS_MISALIGNED;
+    if (launch_prepare(p, plan, phi, gamma, workspace, stream) != 0) return MHC_STATUS_CUDA_ERROR;
+    return run_prepared(p, plan, x, alpha, bias, hIn, hPost, hRes, workspace, stream);
+}
+
 }  // namespace mhc
 
 using namespace mhc;

@@ -64,4 +64,11 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
                void* workspace, cudaStream_t stream, cudaEvent_t evBegin = nullptr, cudaEvent_t evEnd = nullptr);
 int read_and_clear_device_status(int32_t* status);
 
+// Validation + plan for the current device, and prepare-then-run into a given
+// workspace (used by the no-allocation entry point).
+int plan_for(const mhcPreDesc_t* desc, Problem* p, Plan* plan);
+int prepare_and_run(const Problem& p, const Plan& plan, const void* x, const float* phi, const float* alpha,
+                    const float* bias, const float* gamma, void* hIn, float* hPost, float* hRes, void* workspace,
+                    cudaStream_t stream);
+
 }  // namespace mhc
