@@ -7,6 +7,7 @@
 // and replaces the Ascend tiling (core split, M64 matmul tiling, tiling cache)
 // with a B200 launch plan.  It keeps no mutable global state.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
 #include "mhc_pre_internal.h"
@@ -71,18 +72,79 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     if (p.M < kShardRows && pl.tilesM < smCount) splits = std::max(groups, smCount / pl.tilesM);
     splits = std::min(splits, pl.chunks);
     pl.splits = splits;
+    pl.gemmGrid = std::min(pl.tilesM * splits, smCount);
     const size_t stageBytes = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + static_cast<size_t>(p.N) * kChunk * 2;
     const size_t smemLimit = 232448;  // sm_100 per-block opt-in maximum
     const size_t fixed = 1024 /*alignment slack*/ + 256 /*barriers*/;
-    int stages = static_cast<int>((smemLimit - fixed) / stageBytes);
+    // Two GEMM CTAs per SM when their TMEM (3 accumulator buffers of N columns,
+    // rounded to a power of two) fits twice: a single CTA's MMA stream leaves the
+    // tensor core idle between its dependent steps, two interleave.
+    const int accCols = 3 * p.N <= 64 ? 64 : 3 * p.N <= 128 ? 128 : 3 * p.N <= 256 ? 256 : 512;
+    int ctasPerSm = accCols <= 256 ? 2 : 1;
+    if (const char* ct = std::getenv("MHC_PRE_GEMM_CTAS")) ctasPerSm = std::max(1, std::min(std::atoi(ct), 512 / accCols));
+    const size_t budget = ctasPerSm == 1 ? smemLimit : 110 * 1024;
+    int stages = static_cast<int>((budget - fixed) / stageBytes);
     stages = std::max(2, std::min(stages, 8));
+    // Tuning override: MHC_PRE_GEMM_STAGES (ring depth).
+    if (const char* st = std::getenv("MHC_PRE_GEMM_STAGES")) stages = std::max(2, std::min(std::atoi(st), stages));
     pl.stages = stages;
+    pl.gemmGrid = std::min(pl.tilesM * splits, smCount * ctasPerSm);
     pl.smemBytes = fixed + static_cast<size_t>(stages) * stageBytes;
     pl.phiOffset = sizeof(WorkspaceHeader);
     pl.phiBytes = static_cast<size_t>(p.N) * static_cast<size_t>(p.K) * 2;
     pl.partOffset = align_up(pl.phiOffset + pl.phiBytes, 256);
     pl.partBytes = static_cast<size_t>(splits) * static_cast<size_t>(p.M) * static_cast<size_t>(p.W) * 4;
     pl.totalBytes = align_up(pl.partOffset + pl.partBytes, 256);
+
+    // Path 1, the fused kernel, when D splits into 64-wide chunks evenly over a team
+    // (a row's arithmetic depends on the team size S only, not on M).  S divides D/64; it maximises the SMs
+    // used (teams = SMs / S) and, among equals, stays closest to 16.
+    // It is opt-in: MHC_PRE_PATH=1 in the environment selects it.  On B200 its
+    // re-read of x for hIn mostly misses L2, so it moves as many HBM bytes as the
+    // split-K path and runs slower (1.7 ms against 1.3 ms at M=65536, n=4, D=7168).
+    const char* force = std::getenv("MHC_PRE_PATH");
+    const bool want1 = force != nullptr && force[0] == '1';
+    if (want1 && p.D % kChunk == 0) {
+        const int dc = static_cast<int>(p.D / kChunk);
+        int bestS = 0, bestUse = -1;
+        for (int S = 8; S <= 32 && S <= smCount; ++S) {
+            if (dc % S != 0) continue;
+            const int use = (smCount / S) * S;
+            if (use > bestUse || (use == bestUse && std::abs(S - 16) < std::abs(bestS - 16))) {
+                bestS = S;
+                bestUse = use;
+            }
+        }
+        if (bestS == 0 && dc >= 8 && dc <= 32 && dc <= smCount) bestS = dc;  // owners hold <= 16 rows
+        // MHC_PRE_TEAM=<S> forces the team size (tuning); it must divide D/64, 8 <= S <= 64.
+        if (const char* ts = std::getenv("MHC_PRE_TEAM")) {
+            const int fs = std::atoi(ts);
+            if (fs >= 8 && fs <= 64 && fs <= smCount && dc % fs == 0) bestS = fs;
+        }
+        if (bestS > 0) {
+            const int T = std::min(smCount / bestS, pl.tilesM);
+            if (T >= 1) {
+                pl.path = 1;
+                pl.teamS = bestS;
+                pl.teams = T;
+                pl.J = dc / bestS;
+                const size_t gStage = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + static_cast<size_t>(p.N) * kChunk * 2;
+                const size_t hStage = static_cast<size_t>(kRowsPerTile) * kChunk * 2;
+                pl.hStages = p.N <= 48 ? 5 : 4;
+                const size_t fixed = 1024 + 16 * static_cast<size_t>(p.W) * 4 + 512;
+                int gs = static_cast<int>((smemLimit - fixed - pl.hStages * hStage) / gStage);
+                pl.gStages = std::max(2, std::min(gs, 8));
+                pl.smemBytes = fixed + pl.gStages * gStage + pl.hStages * hStage;
+                pl.splits = 1;
+                pl.partOffset = align_up(pl.phiOffset + pl.phiBytes, 256);
+                pl.partBytes = static_cast<size_t>(T) * kFusedSlots * bestS * kRowsPerTile * p.W * 4;
+                pl.hpreOffset = align_up(pl.partOffset + pl.partBytes, 256);
+                pl.cntOffset = align_up(pl.hpreOffset + static_cast<size_t>(T) * kFusedSlots * kRowsPerTile * 8 * 4, 256);
+                pl.cntBytes = align_up((2 * kFusedSlots * static_cast<size_t>(T) + 1) * 4, 256);
+                pl.totalBytes = pl.cntOffset + pl.cntBytes;
+            }
+        }
+    }
     *plan = pl;
     return MHC_STATUS_SUCCESS;
 }
@@ -245,10 +307,11 @@ int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* out) {
     if (rc != 0) return rc;
     std::memset(out, 0, sizeof(*out));
     out->path = plan.path;
-    out->kernelsPerRun = 2;
-    out->gridCtas = plan.tilesM * plan.splits;
-    out->splits = plan.splits;
+    out->kernelsPerRun = plan.path == 1 ? 1 : 2;
+    out->gridCtas = plan.path == 1 ? plan.teams * plan.teamS : plan.gemmGrid;
+    out->splits = plan.path == 1 ? plan.teamS : plan.splits;
     out->rowsPerTile = kRowsPerTile;
+    out->reserved[0] = plan.path == 1 ? plan.teams : 0;
     return MHC_STATUS_SUCCESS;
 }
 

@@ -24,6 +24,7 @@ constexpr uint32_t kPreparedMagic = 0x5048434Du;  // "MCHP"
 constexpr int kRowsPerTile = 128;  // token rows per tensor-core tile (MMA M)
 constexpr int kChunk = 64;         // K elements per TMA box / pipeline stage (128 bytes)
 constexpr int kMaxMix = 80;
+constexpr int kFusedSlots = 2;     // record/hPre slots per team in the fused kernel
 
 // Everything a launch needs, derived once from the description.
 struct Problem {
@@ -42,14 +43,18 @@ struct Problem {
 };
 
 struct Plan {
-    int path;        // 0: split-K GEMM + epilogue kernels
+    int path;        // 0: split-K GEMM + epilogue kernels, 1: fused team kernel
     int tilesM;      // ceil(M / 128)
     int chunks;      // ceil(K / 64)
-    int splits;      // K splits
-    int stages;      // pipeline depth of the GEMM kernel
+    int splits;      // K splits (path 0)
+    int stages;      // pipeline depth of the GEMM kernel (path 0)
+    int gemmGrid;    // persistent CTAs of the GEMM kernel (path 0)
     size_t smemBytes;
     size_t phiOffset, phiBytes;
     size_t partOffset, partBytes;
+    // path 1 (fused): teams of S members, J chunks per stream per member
+    int teamS, teams, J, gStages, hStages;
+    size_t hpreOffset, cntOffset, cntBytes;
     size_t totalBytes;
 };
 

@@ -4,7 +4,7 @@
 //   prepare   phi'[j,k] = gamma[k]*phi[j,k] split into hi + lo 16-bit halves of the x
 //             dtype (fp16: scaled by a power of two into the normal range), stored
 //             [2*mix][K] K-contiguous so TMA can stage it for the tensor cores.
-//   gemm      one CTA per (128-row tile, K split): TMA streams 64-wide K chunks of x
+//   gemm      persistent CTAs over (128-row tile, K split) items: TMA streams 64-wide K chunks of x
 //             and phi' through a shared-memory ring; one thread issues tcgen05.mma
 //             (M=128 token rows, N=2*mix, fp32 accumulators in TMEM); four warps
 //             square-sum the same x chunks from shared memory and add finished
@@ -15,6 +15,7 @@
 //
 // Reference: code/op_kernel/mhc_pre.cpp (the AscendC kernel this replaces).
 #include <algorithm>
+#include <cstdlib>
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -120,6 +121,8 @@ __global__ void prep_split_kernel(const float* __restrict__ phi, const float* __
 // ---------------------------------------------------------------------------
 struct GemmParams {
     int64_t M;
+    int tilesM;
+    int batch;      // chunks issued together by the producer
     int mix;
     int W;
     int chunks;
@@ -129,15 +132,30 @@ struct GemmParams {
     const WorkspaceHeader* hdr;
 };
 
-template <int N>
-struct GemmCfg {
-    static constexpr int kXBytes = kRowsPerTile * kChunk * 2;  // 16 KB
-    static constexpr int kPhiBytes = N * kChunk * 2;          // N rows x 128 B
-    static constexpr int kStageBytes = kXBytes + kPhiBytes;
-    // two accumulator buffers of N fp32 columns each
-    static constexpr uint32_t kTmemCols = 2 * N <= 64 ? 64 : 2 * N <= 128 ? 128 : 2 * N <= 256 ? 256 : 512;
-    static_assert(N % 16 == 0 && N <= 256, "MMA N for M=128 must be a multiple of 16, at most 256");
-};
+
+
+// Adds one finished TMEM accumulator segment (hi columns [0,MIX), lo columns
+// [MIX,2*MIX) at column `col`, this warp's lane quadrant in `lane_base`) into the
+// fp32 running sums.  The loads of a group are all issued before one wait, so a
+// flush costs about one TMEM round trip per group instead of one per 8 columns.
+template <int MIX>
+__device__ __forceinline__ void add_segment(uint32_t lane_base, uint32_t col, float (&run)[MIX]) {
+    constexpr int G = (MIX % 24 == 0) ? 24 : 40;  // columns per group: 24 (mix 24, 48) or 40 (mix 80)
+    static_assert(MIX % G == 0 && G % 8 == 0, "group must tile the mix columns");
+#pragma unroll
+    for (int j0 = 0; j0 < MIX; j0 += G) {
+        uint32_t hi[G], lo[G];
+#pragma unroll
+        for (int k = 0; k < G; k += 8) {
+            tmem_ld_x8(lane_base + col + j0 + k, *reinterpret_cast<uint32_t(*)[8]>(hi + k));
+            tmem_ld_x8(lane_base + col + MIX + j0 + k, *reinterpret_cast<uint32_t(*)[8]>(lo + k));
+        }
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < G; ++t)
+            run[j0 + t] = __fadd_rn(run[j0 + t], __fadd_rn(__uint_as_float(hi[t]), __uint_as_float(lo[t])));
+    }
+}
 
 constexpr int kGemmThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 square-sum + epilogue
 
@@ -147,37 +165,60 @@ constexpr int kGemmThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 square-s
 // K chunks; finished segments are added into IEEE fp32 registers by the epilogue
 // warps while the MMA fills the other accumulator buffer.
 constexpr int kSegChunks = 4;
+// Accumulator buffers: the square-sum warps add segment s-2 into registers while the
+// MMA fills segment s, so they never wait for the tensor core to finish.
+constexpr int kAccBufs = 3;
+constexpr int kFlushLag = kAccBufs - 1;
+
+template <int N>
+struct GemmCfg {
+    static constexpr int kXBytes = kRowsPerTile * kChunk * 2;  // 16 KB
+    static constexpr int kPhiBytes = N * kChunk * 2;          // N rows x 128 B
+    static constexpr int kStageBytes = kXBytes + kPhiBytes;
+    // kAccBufs accumulator buffers of N fp32 columns each
+    static constexpr uint32_t kTmemCols = kAccBufs * N <= 64    ? 64
+                                          : kAccBufs * N <= 128 ? 128
+                                          : kAccBufs * N <= 256 ? 256
+                                                                : 512;
+    static_assert(kAccBufs * N <= 512, "accumulator buffers must fit in TMEM");
+    static_assert(N % 16 == 0 && N <= 256, "MMA N for M=128 must be a multiple of 16, at most 256");
+};
 
 template <int DT, int N>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sumsq_kernel(const __grid_constant__ CUtensorMap xMap, const __grid_constant__ CUtensorMap phiMap,
                       const GemmParams p) {
+    // Persistent: CTA b processes the work items (row tile, K split) b, b+G, b+2G, ...
+    // with one continuous TMA/MMA pipeline, so the SM never drains between items.
     using Cfg = GemmCfg<N>;
     constexpr int MIX = N / 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * Cfg::kStageBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * Cfg::kStageBytes);  // [S]
     uint64_t* empty = full + S;
-    uint64_t* accFull = empty + S;     // [2]
-    uint64_t* accEmpty = accFull + 2;  // [2]
-    uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(accEmpty + 2);
+    uint64_t* accFull = empty + S;            // [kAccBufs]
+    uint64_t* accEmpty = accFull + kAccBufs;  // [kAccBufs]
+    uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(accEmpty + kAccBufs);
     volatile int* abortFlag = reinterpret_cast<volatile int*>(tmemSlot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int tile = blockIdx.x;
-    const int split = blockIdx.y;
-    const int cBegin = static_cast<int>((static_cast<int64_t>(split) * p.chunks) / p.splits);
-    const int cEnd = static_cast<int>((static_cast<int64_t>(split + 1) * p.chunks) / p.splits);
-    const int nChunks = cEnd - cBegin;
+    const int numItems = p.tilesM * p.splits;
+    const int G = gridDim.x;
+    auto item_range = [&](int w, int& tile, int& split, int& cBegin, int& nChunks) {
+        tile = w / p.splits;
+        split = w - tile * p.splits;
+        cBegin = static_cast<int>((static_cast<int64_t>(split) * p.chunks) / p.splits);
+        nChunks = static_cast<int>((static_cast<int64_t>(split + 1) * p.chunks) / p.splits) - cBegin;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1 + 4);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kAccBufs; ++b) {
             mbar_init(&accFull[b], 1);
             mbar_init(&accEmpty[b], 4);
         }
@@ -206,57 +247,79 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         *abortFlag = 1;
     };
 
-    if (prepared && nChunks > 0) {
+    if (prepared) {
         if (warp == 0) {
             if (lane == 0) {
-                int issued = 0;
-                for (int i = 0; i < nChunks; ++i) {
-                    const int s = i % S;
-                    const uint32_t use = static_cast<uint32_t>(i / S);
-                    if (i >= S && !mbar_wait(&empty[s], (use & 1u) ^ 1u, abortFlag)) {
-                        fail();
-                        break;
+                int g = 0;
+                const int batch = p.batch;
+                for (int w = blockIdx.x; w < numItems && !*abortFlag; w += G) {
+                    int tile, split, cBegin, nChunks;
+                    item_range(w, tile, split, cBegin, nChunks);
+                    // Chunks are issued in batches of consecutive K ranges, so that each
+                    // row's neighbouring 128-byte segments reach DRAM close together.
+                    for (int i0 = 0; i0 < nChunks && !*abortFlag; i0 += batch) {
+                        const int nb = min(batch, nChunks - i0);
+                        bool okb = true;
+                        for (int u = 0; u < nb; ++u) {
+                            const int gg = g + u;
+                            if (gg >= S && !mbar_wait(&empty[gg % S], (static_cast<uint32_t>(gg / S) & 1u) ^ 1u, abortFlag)) {
+                                fail();
+                                okb = false;
+                                break;
+                            }
+                        }
+                        if (!okb) break;
+                        for (int u = 0; u < nb; ++u, ++g) {
+                            const int s = g % S;
+                            mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+                            const int kc = (cBegin + i0 + u) * kChunk;
+                            tma_load_2d(stage_x(s), &xMap, &full[s], kc, tile * kRowsPerTile);
+                            tma_load_2d(stage_phi(s), &phiMap, &full[s], kc, 0);
+                        }
                     }
-                    mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-                    const int kc = (cBegin + i) * kChunk;
-                    tma_load_2d(stage_x(s), &xMap, &full[s], kc, tile * kRowsPerTile);
-                    tma_load_2d(stage_phi(s), &phiMap, &full[s], kc, 0);
-                    issued = i + 1;
                 }
                 if (*abortFlag != 0) {
                     // Let copies already in flight land before the CTA exits (bounded).
-                    for (int i = (issued > S ? issued - S : 0); i < issued; ++i) {
-                        mbar_wait(&full[i % S], static_cast<uint32_t>(i / S) & 1u, nullptr, 100000000ull);
-                    }
+                    for (int k = (g > S ? g - S : 0); k < g; ++k)
+                        mbar_wait(&full[k % S], static_cast<uint32_t>(k / S) & 1u, nullptr, 100000000ull);
                 }
             }
         } else if (warp == 1) {
             if (lane == 0) {
                 constexpr uint32_t idesc = idesc_f16(DT, kRowsPerTile, N);
-                for (int i = 0; i < nChunks; ++i) {
-                    const int s = i % S;
-                    const int seg = i / kSegChunks;
-                    const int b = seg & 1;
-                    if (i % kSegChunks == 0 && seg >= 2 &&
-                        !mbar_wait(&accEmpty[b], static_cast<uint32_t>((seg >> 1) - 1) & 1u, abortFlag)) {
-                        fail();
-                        break;
-                    }
-                    if (!mbar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u, abortFlag)) {
-                        fail();
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a0 = smem_u32(stage_x(s));
-                    const uint32_t b0 = smem_u32(stage_phi(s));
-                    const uint32_t d = tacc + static_cast<uint32_t>(b * N);
+                int g = 0, segBase = 0;
+                bool ok = true;
+                for (int w = blockIdx.x; w < numItems && ok; w += G) {
+                    int tile, split, cBegin, nChunks;
+                    item_range(w, tile, split, cBegin, nChunks);
+                    for (int i = 0; i < nChunks; ++i, ++g) {
+                        const int s = g % S;
+                        const int seg = segBase + i / kSegChunks;
+                        const int b = seg % kAccBufs;
+                        if (i % kSegChunks == 0 && seg >= kAccBufs &&
+                            !mbar_wait(&accEmpty[b], static_cast<uint32_t>(seg / kAccBufs - 1) & 1u, abortFlag)) {
+                            fail();
+                            ok = false;
+                            break;
+                        }
+                        if (!mbar_wait(&full[s], static_cast<uint32_t>(g / S) & 1u, abortFlag)) {
+                            fail();
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a0 = smem_u32(stage_x(s));
+                        const uint32_t b0 = smem_u32(stage_phi(s));
+                        const uint32_t d = tacc + static_cast<uint32_t>(b * N);
 #pragma unroll
-                    for (int k16 = 0; k16 < kChunk / 16; ++k16) {
-                        mma_f16_ss(d, sdesc_sw128(a0 + k16 * 32), sdesc_sw128(b0 + k16 * 32), idesc,
-                                   (i % kSegChunks != 0 || k16 > 0) ? 1u : 0u);
+                        for (int k16 = 0; k16 < kChunk / 16; ++k16) {
+                            mma_f16_ss(d, sdesc_sw128(a0 + k16 * 32), sdesc_sw128(b0 + k16 * 32), idesc,
+                                       (i % kSegChunks != 0 || k16 > 0) ? 1u : 0u);
+                        }
+                        mma_commit(&empty[s]);
+                        if (i % kSegChunks == kSegChunks - 1 || i == nChunks - 1) mma_commit(&accFull[b]);
                     }
-                    mma_commit(&empty[s]);
-                    if (i % kSegChunks == kSegChunks - 1 || i == nChunks - 1) mma_commit(&accFull[b]);
+                    segBase += (nChunks + kSegChunks - 1) / kSegChunks;
                 }
             }
         } else {
@@ -265,68 +328,66 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int row = q * 32 + lane;
             const uint32_t lane_base = tacc + (static_cast<uint32_t>(q * 32) << 16);
             float run[MIX];
-#pragma unroll
-            for (int j = 0; j < MIX; ++j) run[j] = 0.0f;
-            bool ok = true;
             // Adds finished accumulator segment `seg` into run[] and frees its buffer.
             auto flush = [&](int seg) -> bool {
-                const int b = seg & 1;
+                const int b = seg % kAccBufs;
                 // warp-uniform outcome: the TMEM loads below are warp-collective
-                if (!__all_sync(0xffffffffu, mbar_wait(&accFull[b], static_cast<uint32_t>(seg >> 1) & 1u, abortFlag)))
+                if (!__all_sync(0xffffffffu,
+                                mbar_wait(&accFull[b], static_cast<uint32_t>(seg / kAccBufs) & 1u, abortFlag)))
                     return false;
                 tc_fence_after();
-#pragma unroll
-                for (int j0 = 0; j0 < MIX; j0 += 8) {
-                    uint32_t hi[8], lo[8];
-                    tmem_ld_x8(lane_base + b * N + j0, hi);
-                    tmem_ld_x8(lane_base + b * N + MIX + j0, lo);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) {
-                        run[j0 + t] =
-                            __fadd_rn(run[j0 + t], __fadd_rn(__uint_as_float(hi[t]), __uint_as_float(lo[t])));
-                    }
-                }
+                add_segment<MIX>(lane_base, static_cast<uint32_t>(b * N), run);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&accEmpty[b]);
                 return true;
             };
-            float ss = 0.0f;
-            for (int i = 0; i < nChunks; ++i) {
-                const int s = i % S;
-                if (!__all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>(i / S) & 1u, abortFlag))) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t base = smem_u32(stage_x(s)) + row * 128;
-                float part = 0.0f;
+            const float unscale = ldexpf(1.0f, -p.hdr->phiScaleExp);
+            int g = 0, segBase = 0;
+            bool ok = true;
+            for (int w = blockIdx.x; w < numItems && ok; w += G) {
+                int tile, split, cBegin, nChunks;
+                item_range(w, tile, split, cBegin, nChunks);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint4 v = lds128(base + ((j ^ (row & 7)) << 4));
-                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        const float2 f = x2_to_f32<DT>(w[t]);
-                        part = fmaf(f.x, f.x, part);
-                        part = fmaf(f.y, f.y, part);
-                    }
-                }
-                ss += part;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
-                const int seg = i / kSegChunks;
-                if ((i % kSegChunks == kSegChunks - 1 || i == nChunks - 1) && seg >= 1) {
-                    if (!flush(seg - 1)) {
+                for (int j = 0; j < MIX; ++j) run[j] = 0.0f;
+                float ss = 0.0f;
+                for (int i = 0; i < nChunks; ++i, ++g) {
+                    const int s = g % S;
+                    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>(g / S) & 1u, abortFlag))) {
                         ok = false;
                         break;
                     }
+                    const uint32_t base = smem_u32(stage_x(s)) + row * 128;
+                    float part = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint4 v = lds128(base + ((j ^ (row & 7)) << 4));
+                        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const float2 f = x2_to_f32<DT>(wv[t]);
+                            part = fmaf(f.x, f.x, part);
+                            part = fmaf(f.y, f.y, part);
+                        }
+                    }
+                    ss += part;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[s]);
+                    const int segL = i / kSegChunks;
+                    if ((i % kSegChunks == kSegChunks - 1 || i == nChunks - 1) && segL >= kFlushLag) {
+                        if (!flush(segBase + segL - kFlushLag)) {
+                            ok = false;
+                            break;
+                        }
+                    }
                 }
-            }
-            ok = __all_sync(0xffffffffu, ok);
-            if (ok) ok = __all_sync(0xffffffffu, flush((nChunks - 1) / kSegChunks));
-            if (ok) {
-                const float unscale = ldexpf(1.0f, -p.hdr->phiScaleExp);
+                {
+                    // the item's remaining segments (the last kFlushLag, or fewer)
+                    const int nSeg = (nChunks + kSegChunks - 1) / kSegChunks;
+                    for (int sg = max(0, nSeg - kFlushLag); sg < nSeg && ok; ++sg) ok = flush(segBase + sg);
+                }
+                segBase += (nChunks + kSegChunks - 1) / kSegChunks;
+                if (!ok) break;
                 const int64_t grow = static_cast<int64_t>(tile) * kRowsPerTile + row;
                 if (grow < p.M) {
                     float* out = p.partials + (static_cast<int64_t>(split) * p.M + grow) * p.W;
@@ -341,9 +402,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                     out[MIX] = ss;
                 }
-            } else if (lane == 0) {
-                fail();
             }
+            if (!ok && lane == 0) fail();
         }
     }
 
@@ -462,6 +522,8 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
     }
 }
 
+#include "mhc_pre_fused.cuh"
+
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
@@ -491,8 +553,7 @@ static int launch_gemm(const Plan& plan, const CUtensorMap& xMap, const CUtensor
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(plan.smemBytes));
     if (e != cudaSuccess) return e;
-    dim3 grid(plan.tilesM, plan.splits);
-    kern<<<grid, kGemmThreads, plan.smemBytes, stream>>>(xMap, phiMap, gp);
+    kern<<<plan.gemmGrid, kGemmThreads, plan.smemBytes, stream>>>(xMap, phiMap, gp);
     return cudaGetLastError();
 }
 
@@ -502,11 +563,86 @@ static int launch_epi(const Problem& p, const EpiParams& ep, cudaStream_t stream
     return cudaGetLastError();
 }
 
+template <int DT, int NS>
+static int launch_fused_t(const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap, const FusedParams& fp,
+                          cudaStream_t stream) {
+    auto kern = mhc_pre_fused_kernel<DT, NS>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(plan.smemBytes));
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.teams * plan.teamS), 1, 1);
+    cfg.blockDim = dim3(kFusedThreads, 1, 1);
+    cfg.dynamicSmemBytes = plan.smemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA co-resident: teams wait on each other
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, xMap, phiMap, fp);
+}
+
+static int launch_fused(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
+                        const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes, void* workspace,
+                        cudaStream_t stream, cudaEvent_t evBegin, cudaEvent_t evEnd) {
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaError_t e = cudaMemsetAsync(ws + plan.cntOffset, 0, plan.cntBytes, stream);
+    if (e != cudaSuccess) return e;
+    FusedParams fp;
+    fp.M = p.M;
+    fp.D = p.D;
+    fp.J = plan.J;
+    fp.S = plan.teamS;
+    fp.T = plan.teams;
+    fp.tilesM = plan.tilesM;
+    fp.W = p.W;
+    fp.gStages = plan.gStages;
+    fp.hStages = plan.hStages;
+    {
+        const char* hm = std::getenv("MHC_PRE_L2HINT");  // tuning override: 0, 1 or 2
+        fp.l2mode = hm != nullptr ? std::atoi(hm) : 1;
+    }
+    fp.invK = 1.0f / static_cast<float>(p.K);
+    fp.normEps = p.normEps;
+    fp.hcEps = p.hcEps;
+    fp.alpha = alpha;
+    fp.bias = bias;
+    fp.hIn = static_cast<uint16_t*>(hIn);
+    fp.hPost = hPost;
+    fp.hRes = hRes;
+    fp.part = reinterpret_cast<float*>(ws + plan.partOffset);
+    fp.hpre = reinterpret_cast<float*>(ws + plan.hpreOffset);
+    fp.cnt = reinterpret_cast<unsigned*>(ws + plan.cntOffset);
+    fp.hdr = reinterpret_cast<const WorkspaceHeader*>(workspace);
+    if (evBegin != nullptr && cudaEventRecord(evBegin, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    const bool bf = p.dtype == MHC_DTYPE_BF16;
+    int rc;
+    switch (p.n) {
+        case 4: rc = bf ? launch_fused_t<MHC_DTYPE_BF16, 4>(plan, xMap, phiMap, fp, stream)
+                        : launch_fused_t<MHC_DTYPE_F16, 4>(plan, xMap, phiMap, fp, stream); break;
+        case 6: rc = bf ? launch_fused_t<MHC_DTYPE_BF16, 6>(plan, xMap, phiMap, fp, stream)
+                        : launch_fused_t<MHC_DTYPE_F16, 6>(plan, xMap, phiMap, fp, stream); break;
+        default: rc = bf ? launch_fused_t<MHC_DTYPE_BF16, 8>(plan, xMap, phiMap, fp, stream)
+                         : launch_fused_t<MHC_DTYPE_F16, 8>(plan, xMap, phiMap, fp, stream); break;
+    }
+    if (rc != 0) return rc;
+    if (evEnd != nullptr && cudaEventRecord(evEnd, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    return 0;
+}
+
 int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
                const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
                void* workspace, cudaStream_t stream, cudaEvent_t evBegin, cudaEvent_t evEnd) {
+    if (plan.path == 1)
+        return launch_fused(p, plan, xMap, phiMap, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
     GemmParams gp;
     gp.M = p.M;
+    gp.tilesM = plan.tilesM;
+    {
+        const char* b = std::getenv("MHC_PRE_BATCH");  // tuning override
+        gp.batch = b != nullptr ? std::max(1, std::min(std::atoi(b), plan.stages)) : std::min(4, plan.stages / 2);
+    }
     gp.mix = p.mix;
     gp.W = p.W;
     gp.chunks = plan.chunks;

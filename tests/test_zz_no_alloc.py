@@ -110,7 +110,9 @@ def test_no_alloc_entry_matches_workspace_entry_twice():
 
 
 def test_no_alloc_rejects_problems_larger_than_the_scratch_array():
-    cfg = with_shape(CONFIGS["c4"], batch=32)  # M = 131072: workspace ~ 106 MB > 64 MiB
+    # D = 7184 is not a multiple of 64, so this runs on the split-K path, whose
+    # partial records grow with M: about 117 MB of workspace at M = 131072
+    cfg = with_shape(CONFIGS["c4"], batch=32, D=7184)
     d = mp.make_desc(cfg.batch, cfg.seq, cfg.n, cfg.D, mp.BF16, True)
     assert mp.workspace_size(d) > 64 * 1024 * 1024
     rc = mp.lib().mhcPreRunNoAlloc(ctypes.byref(d), None, None, None, None, None, None, None, None, _stream())
