@@ -23,6 +23,16 @@ The JSON line also carries:
   clocks        nvidia-smi samples taken during the timed region.
 --impl reference times the reference's own CPU formula (the oracle port; the
 reference itself is AscendC for Ascend 910B and cannot run here) on all host cores.
+
+    python bench.py --decode-sweep [--steps K]
+
+prints instead one JSON line with BASELINE config 5: the p50 latency of one MhcPre
+call for M in {1, 8, 32, 128, 512}, n=4, D=7168, fp16, gamma on and off, with L2
+flushed before every call (a 256 MB write) and without the flush.  "graph" is the
+call captured once in a CUDA graph and replayed (CUDA events around each replay:
+device time only); "eager" is the call itself between the events, so it includes
+the host's launch work whenever that is slower than the kernels; "host_us" is the
+host time of one eager call.
 """
 from __future__ import annotations
 
@@ -53,6 +63,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--batch", type=int, default=0, help="override the config's batch (profiling cases)")
+    ap.add_argument("--decode-sweep", action="store_true", help="config 5 latency sweep (its own JSON line)")
     return ap.parse_args()
 
 
@@ -292,8 +303,66 @@ def measure_e2e(mp, inp, cfg, steps, pg, dist, world):
             "ms_per_step": ms, "chunks": chunks, "pinned_host": True}
 
 
+def decode_sweep(args):
+    """p50 latency per M, flushed and unflushed L2."""
+    import torch
+    import mhcpre_review_b200 as mp
+    from mhcpre_review_b200.configs import CONFIGS, make_inputs
+    torch.cuda.set_device(0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    steps = max(args.steps, 20)
+    results = []
+    for m in (1, 8, 32, 128, 512):
+        for g in (True, False):
+            cfg = CONFIGS[f"c5_m{m}_{'g' if g else 'ng'}"]
+            inp = make_inputs(cfg)
+            ex = mp.MhcPre(cfg.batch, cfg.seq, cfg.n, cfg.D, inp["x"].dtype, cfg.gamma, cfg.norm_eps, cfg.hc_eps)
+            ex.prepare(inp["phi"], inp["gamma"])
+            out = ex.outputs(inp["x"].dtype)
+            row = {"M": m, "gamma": g, "plan": ex.plan}
+            for _ in range(max(args.warmup, 3)):
+                ex(inp["x"], inp["alpha"], inp["bias"], out=out)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(200):
+                ex(inp["x"], inp["alpha"], inp["bias"], out=out)
+            row["host_us"] = (time.perf_counter() - t0) / 200 * 1e6
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                ex(inp["x"], inp["alpha"], inp["bias"], out=out)
+            for mode in ("eager", "graph"):
+                call = graph.replay if mode == "graph" else (lambda: ex(inp["x"], inp["alpha"], inp["bias"], out=out))
+                for flushed in (True, False):
+                    for _ in range(max(args.warmup, 3)):
+                        call()
+                    ts = []
+                    for _ in range(steps):
+                        if flushed:
+                            flush.fill_(1)
+                        b = torch.cuda.Event(enable_timing=True)
+                        e = torch.cuda.Event(enable_timing=True)
+                        b.record()
+                        call()
+                        e.record()
+                        torch.cuda.synchronize()
+                        ts.append(b.elapsed_time(e) * 1e3)
+                    ts.sort()
+                    row[f"p50_us_{mode}_{'flushed' if flushed else 'warm'}"] = ts[len(ts) // 2]
+            del graph
+            row["algorithmic_bytes"] = cfg.algorithmic_bytes()
+            results.append(row)
+            if mp.device_status() != 0:
+                raise RuntimeError("device status")
+    print(json.dumps({"metric": "MhcPre decode latency (BASELINE config 5)", "unit": "us", "stat": "p50",
+                      "steps": steps, "results": results}), flush=True)
+
+
 def main():
     args = parse()
+    if args.decode_sweep:
+        decode_sweep(args)
+        return
     world, rank, local = dist_env()
     from mhcpre_review_b200.configs import CONFIGS, with_shape as _ws
     cfg = CONFIGS[args.config]

@@ -57,6 +57,7 @@ static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 constexpr int kGroupChunks = 64;      // 4096 K elements per split for large M
 constexpr int64_t kShardRows = 8192;  // from this M up, splits depend on K only
+constexpr int kMinSplitChunks = 6;    // smallest split below kShardRows rows
 
 int make_plan(const Problem& p, int smCount, Plan* plan) {
     Plan pl{};
@@ -66,10 +67,13 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     // K splits.  From kShardRows rows up, the split count depends on K only (groups
     // of at most kGroupChunks chunks), so a row's arithmetic, and therefore its
     // result bits, do not depend on M: token shards of that size reproduce the
-    // unsharded run exactly.  Smaller problems split further to fill the SMs.
+    // unsharded run exactly.  Smaller problems split further to fill the SMs, down
+    // to kMinSplitChunks chunks per split: below that the epilogue's reduction over
+    // splits costs more than the GEMM CTAs save.
     const int groups = (pl.chunks + kGroupChunks - 1) / kGroupChunks;
     int splits = groups;
-    if (p.M < kShardRows && pl.tilesM < smCount) splits = std::max(groups, smCount / pl.tilesM);
+    if (p.M < kShardRows && pl.tilesM < smCount)
+        splits = std::max(groups, std::min(smCount / pl.tilesM, std::max(1, pl.chunks / kMinSplitChunks)));
     splits = std::min(splits, pl.chunks);
     pl.splits = splits;
     pl.gemmGrid = std::min(pl.tilesM * splits, smCount);
@@ -97,24 +101,36 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     pl.totalBytes = align_up(pl.partOffset + pl.partBytes, 256);
 
     // Path 1, the fused kernel, when D splits into 64-wide chunks evenly over a team
-    // (a row's arithmetic depends on the team size S only, not on M).  S divides D/64; it maximises the SMs
-    // used (teams = SMs / S) and, among equals, stays closest to 16.
-    // It is opt-in: MHC_PRE_PATH=1 in the environment selects it.  On B200 its
-    // re-read of x for hIn mostly misses L2, so it moves as many HBM bytes as the
-    // split-K path and runs slower (1.7 ms against 1.3 ms at M=65536, n=4, D=7168).
+    // (a row's arithmetic depends on the team size S only, not on M).  S divides
+    // D/64.  Its hIn pass re-reads x from L2, which can hit only while the tiles the
+    // teams have in flight fit in L2; S is the smallest divisor that keeps one round
+    // of tiles (one per team) under kFusedFootprint among those using the most SMs,
+    // else the largest divisor.
+    // It is opt-in (MHC_PRE_PATH=1 in the environment): on B200 one team handshake
+    // (records, owner reduction, hPre) takes tens of microseconds while every SM
+    // streams, because each step queues behind the SM's TMA traffic; a byte of x then
+    // waits ~80 us for its re-read, far more than L2 holds at full bandwidth, so the
+    // re-read mostly misses and the kernel runs slower than the split-K path.
     const char* force = std::getenv("MHC_PRE_PATH");
     const bool want1 = force != nullptr && force[0] == '1';
     if (want1 && p.D % kChunk == 0) {
         const int dc = static_cast<int>(p.D / kChunk);
+        const double tileBytes = static_cast<double>(kRowsPerTile) * static_cast<double>(p.K) * 2.0;
+        constexpr double kFusedFootprint = 40.0e6;
         int bestS = 0, bestUse = -1;
-        for (int S = 8; S <= 32 && S <= smCount; ++S) {
+        for (int S = 8; S <= 64 && S <= smCount; ++S) {
             if (dc % S != 0) continue;
-            const int use = (smCount / S) * S;
-            if (use > bestUse || (use == bestUse && std::abs(S - 16) < std::abs(bestS - 16))) {
+            const int teams = std::min<int64_t>(smCount / S, pl.tilesM);
+            if (teams * tileBytes > kFusedFootprint) continue;
+            const int use = teams * S;
+            if (use > bestUse) {
                 bestS = S;
                 bestUse = use;
             }
         }
+        if (bestS == 0)
+            for (int S = 8; S <= 64 && S <= smCount; ++S)
+                if (dc % S == 0) bestS = S;
         if (bestS == 0 && dc >= 8 && dc <= 32 && dc <= smCount) bestS = dc;  // owners hold <= 16 rows
         // MHC_PRE_TEAM=<S> forces the team size (tuning); it must divide D/64, 8 <= S <= 64.
         if (const char* ts = std::getenv("MHC_PRE_TEAM")) {
@@ -131,7 +147,8 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
                 const size_t gStage = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + static_cast<size_t>(p.N) * kChunk * 2;
                 const size_t hStage = static_cast<size_t>(kRowsPerTile) * kChunk * 2;
                 pl.hStages = p.N <= 48 ? 5 : 4;
-                const size_t fixed = 1024 + 16 * static_cast<size_t>(p.W) * 4 + 512;
+                const size_t ownBytes = static_cast<size_t>((kRowsPerTile + bestS - 1) / bestS) * bestS * p.W * 4;
+                const size_t fixed = 1024 + 16 * static_cast<size_t>(p.W) * 4 + ownBytes + 512;
                 int gs = static_cast<int>((smemLimit - fixed - pl.hStages * hStage) / gStage);
                 pl.gStages = std::max(2, std::min(gs, 8));
                 pl.smemBytes = fixed + pl.gStages * gStage + pl.hStages * hStage;
@@ -168,13 +185,20 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-static EncodeTiledFn get_encode_fn() {
+static EncodeTiledFn lookup_encode_fn() {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q{};
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
         q != cudaDriverEntryPointSuccess)
         return nullptr;
     return reinterpret_cast<EncodeTiledFn>(fn);
+}
+
+// The driver entry point, looked up once per process (the lookup costs microseconds
+// per call otherwise).
+static EncodeTiledFn get_encode_fn() {
+    static const EncodeTiledFn fn = lookup_encode_fn();
+    return fn;
 }
 
 // 2-D K-contiguous matrix [rows][K] of 16-bit elements, 64 x boxRows boxes,

@@ -9,13 +9,19 @@
 //      segments that warps 4-7 add into fp32 registers, which also square-sum x;
 //   2. publishes its partial records (mix sums + sum of squares per row) in a global
 //      buffer and bumps the team's counter (release);
-//   3. as the owner of R/S rows (warp 3), sums the S members' records in member
-//      order (so the result does not depend on timing), computes invRms, hPre, hPost,
-//      hRes, writes hPost/hRes and publishes hPre (release);
+//   3. as the owner of R/S rows (warp 3), fetches those rows' records of all S
+//      members with one bulk copy per row (records are stored row-major, members
+//      inner), sums them in member order (so the result does not depend on timing),
+//      computes invRms, hPre, hPost, hRes, writes hPost/hRes and publishes hPre
+//      (release);
 //   4. re-reads its chunks of the tile through a second TMA ring (an L2 hit: the
 //      first read was moments ago) and forms hIn for its slice from hPre.
 // Step 4 of tile i (warps 8-11) overlaps steps 1-2 of tile i+1 (warps 0-1, 4-7) and
-// step 3 of tile i+1 (warp 3).
+// step 3 of tile i+1 (warp 3).  The re-read can hit L2 only while the data that all
+// teams stream between a tile's first read and its re-read fits in L2; the host
+// picks a team size for which one round of tiles stays under 40 MB.  Measured on
+// B200, the handshake of steps 2-3 takes tens of microseconds while every SM
+// streams, so most re-reads still miss and this path is opt-in.
 // Every wait is bounded; a timeout sets the device status word and a team-wide
 // abort word, and all roles wind down.
 // It is included inside namespace mhc after the path-0 kernels, whose helpers
@@ -41,7 +47,7 @@ struct FusedParams {
     uint16_t* hIn;
     float* hPost;
     float* hRes;
-    float* part;     // [T][2][S][128][W]
+    float* part;     // [T][kSlots][128][S][W]
     float* hpre;     // [T][2][128][8]
     unsigned* cnt;   // [T][2*kSlots]: record arrivals per slot, then hPre arrivals per slot; [2*kSlots*T]: abort word
     const WorkspaceHeader* hdr;
@@ -117,7 +123,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     uint8_t* gRing = smem;
     uint8_t* hRing = gRing + static_cast<size_t>(GS) * Cfg::kGStageBytes;
     float* sTot = reinterpret_cast<float*>(hRing + static_cast<size_t>(HS) * kHinStageBytes);  // [16][W]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sTot + 16 * p.W);
+    const int ownRows = (kRowsPerTile + p.S - 1) / p.S;
+    float* ownBuf = sTot + 16 * p.W;  // [ownRows][S][W]: the owned rows' records of all members
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ownBuf + static_cast<size_t>(ownRows) * p.S * p.W);
     uint64_t* gFull = bars;
     uint64_t* gEmpty = gFull + GS;
     uint64_t* hFull = gEmpty + GS;
@@ -125,7 +133,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     uint64_t* accFull = hEmpty + HS;   // [2]
     uint64_t* accEmpty = accFull + 2;  // [2]
     uint64_t* hpreTaken = accEmpty + 2;  // [kSlots]
-    uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(hpreTaken + kSlots);
+    uint64_t* ownBar = hpreTaken + kSlots;
+    uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(ownBar + 1);
     volatile int* abortFlag = reinterpret_cast<volatile int*>(tmemSlot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -135,7 +144,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     const int nLocal = team < p.tilesM ? (p.tilesM - 1 - team) / p.T + 1 : 0;
     const int nq = p.J * NS;  // chunks per tile
     const int segPerTile = (nq + kSegChunks - 1) / kSegChunks;
-    const int ownRows = (kRowsPerTile + p.S - 1) / p.S;
     const int ownBase = member * ownRows;
     const int ownCount = max(0, min(ownRows, kRowsPerTile - ownBase));
     unsigned* cntT = p.cnt + 2 * kSlots * team;
@@ -155,6 +163,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             mbar_init(&accEmpty[b], 4);
         }
         for (int b = 0; b < kSlots; ++b) mbar_init(&hpreTaken[b], 4);
+        mbar_init(ownBar, 1);
         *abortFlag = 0;
         fence_mbarrier_init();
     }
@@ -330,8 +339,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                     ok = __all_sync(0xffffffffu, mbar_wait(&hpreTaken[i % kSlots],
                                                            static_cast<uint32_t>(i / kSlots - 1) & 1u, abortFlag));
                 if (ok) {
-                    float* rec = p.part + ((((static_cast<int64_t>(team) * kSlots + (i % kSlots)) * p.S + member) *
-                                                kRowsPerTile + row) * p.W);
+                    float* rec = p.part + ((((static_cast<int64_t>(team) * kSlots + (i % kSlots)) * kRowsPerTile + row) *
+                                                p.S + member) * p.W);
 #pragma unroll
                     for (int j0 = 0; j0 < MIX; j0 += 4) {
                         float4 a;
@@ -342,6 +351,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                         *reinterpret_cast<float4*>(rec + j0) = a;
                     }
                     rec[MIX] = ss;
+                    fence_proxy_async();  // the owners read the records with bulk copies
                     __threadfence();
                 }
                 // all four warps agree before the release (no warp may be left waiting)
@@ -357,7 +367,6 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
             // hIn streaming of the previous tile.
             const float a0 = __ldg(p.alpha + 0), a1 = __ldg(p.alpha + 1), a2 = __ldg(p.alpha + 2);
             const int w4 = p.W / 4;
-            const int64_t mstride = static_cast<int64_t>(kRowsPerTile) * p.W;
             for (int i = 0; i < nLocal; ++i) {
                 const int tile = team + i * p.T;
                 const int slot = i % kSlots;
@@ -368,31 +377,41 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
                     if (lane == 0) fail();
                     break;
                 }
-                // (b) sum the records over members, in member order; each lane takes 4
-                // columns of one owned row and loads 8 members at a time
-                const float* recs = p.part + (static_cast<int64_t>(team) * kSlots + slot) * p.S * kRowsPerTile * p.W;
-                for (int idx = lane; idx < ownCount * w4; idx += 32) {
-                    const int r = idx / w4;
-                    const int j = (idx - r * w4) * 4;
-                    const float* src = recs + static_cast<int64_t>(ownBase + r) * p.W + j;
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int m0 = 0; m0 < p.S; m0 += 8) {
-                        float4 v[8];
-#pragma unroll
-                        for (int u = 0; u < 8; ++u)
-                            v[u] = (m0 + u < p.S) ? __ldcg(reinterpret_cast<const float4*>(src + (m0 + u) * mstride))
-                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) {
-                            if (m0 + u < p.S) {
-                                acc.x = __fadd_rn(acc.x, v[u].x);
-                                acc.y = __fadd_rn(acc.y, v[u].y);
-                                acc.z = __fadd_rn(acc.z, v[u].z);
-                                acc.w = __fadd_rn(acc.w, v[u].w);
-                            }
+                // (b) the owned rows' records of every member, one bulk copy per row, then
+                // the sum over members in member order; each lane takes 4 columns of a row
+                if (ownCount > 0) {
+                    const int64_t rowFloats = static_cast<int64_t>(p.S) * p.W;
+                    const float* recs =
+                        p.part + ((static_cast<int64_t>(team) * kSlots + slot) * kRowsPerTile + ownBase) * rowFloats;
+                    fence_proxy_async();  // acquired records, and last tile's reads of ownBuf, before the copies
+                    if (lane == 0) mbar_arrive_expect_tx(ownBar, static_cast<uint32_t>(rowFloats * 4 * ownCount));
+                    __syncwarp();
+                    if (lane < ownCount)
+                        bulk_load(ownBuf + lane * rowFloats, recs + lane * rowFloats, static_cast<uint32_t>(rowFloats * 4),
+                                  ownBar);
+                    if (!__all_sync(0xffffffffu, mbar_wait(ownBar, static_cast<uint32_t>(i) & 1u, abortFlag))) {
+                        if (lane == 0) {
+                            fail();
+                            // let the copies in flight land before the CTA can exit (bounded)
+                            mbar_wait(ownBar, static_cast<uint32_t>(i) & 1u, nullptr, 100000000ull);
                         }
+                        __syncwarp();
+                        break;
                     }
-                    *reinterpret_cast<float4*>(sTot + r * p.W + j) = acc;
+                    for (int idx = lane; idx < ownCount * w4; idx += 32) {
+                        const int r = idx / w4;
+                        const int j = (idx - r * w4) * 4;
+                        const float* src = ownBuf + r * rowFloats + j;
+                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int m = 0; m < p.S; ++m) {
+                            const float4 v = *reinterpret_cast<const float4*>(src + m * p.W);
+                            acc.x = __fadd_rn(acc.x, v.x);
+                            acc.y = __fadd_rn(acc.y, v.y);
+                            acc.z = __fadd_rn(acc.z, v.z);
+                            acc.w = __fadd_rn(acc.w, v.w);
+                        }
+                        *reinterpret_cast<float4*>(sTot + r * p.W + j) = acc;
+                    }
                 }
                 __syncwarp();
                 // (c) epilogue of the owned rows: hPost/hRes out, hPre published

@@ -15,6 +15,7 @@
 //
 // Reference: code/op_kernel/mhc_pre.cpp (the AscendC kernel this replaces).
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 
 #include <cuda_bf16.h>
@@ -236,6 +237,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // the epilogue grid may start launching now; it waits for this grid in-kernel
+    grid_launch_dependents();
     const uint32_t tacc = *tmemSlot;
     const bool prepared = p.hdr->magic == kPreparedMagic;
     if (!prepared && threadIdx.x == 0) set_device_status(MHC_STATUS_NOT_PREPARED);
@@ -439,6 +442,9 @@ struct EpiParams {
 };
 
 constexpr int kEpiThreads = 128;
+// Splits whose partial records the epilogue stages in shared memory at a time: the
+// loads of a block are all in flight together instead of one split after another.
+constexpr int kEpiSplitBlock = 48;
 
 // sigmoid(v) = 1 / (1 + exp(-v)), in the operation order of the reference's
 // Sigmoid helper (code/op_kernel/mhc_pre.cpp:542-555).
@@ -449,21 +455,38 @@ __device__ __forceinline__ float sigmoid_ref(float v) {
     return __fdiv_rn(1.0f, t);
 }
 
+// Launched as a programmatic dependent of the GEMM: it waits for the GEMM's
+// completion (and memory) before reading the partial records.  Dynamic shared
+// memory: min(splits, kEpiSplitBlock) * (mix + 1) floats.
 template <int DT, int NS>
 __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiParams p) {
     constexpr int mix = NS * NS + 2 * NS;
+    constexpr int cols = mix + 1;
+    extern __shared__ float sPart[];  // [block split][cols]
     __shared__ float sMix[mix];
     __shared__ float sPre[NS];
     __shared__ float sSum;
     const int64_t r = blockIdx.x;
     const int tid = threadIdx.x;
-    if (tid <= mix) {
-        float acc = 0.0f;
-        for (int sp = 0; sp < p.splits; ++sp) {
-            acc = __fadd_rn(acc, p.partials[(static_cast<int64_t>(sp) * p.M + r) * p.W + tid]);
+    grid_dependency_wait();
+    // sum over splits in split order, staged kEpiSplitBlock splits at a time
+    float acc = 0.0f;
+    for (int sp0 = 0; sp0 < p.splits; sp0 += kEpiSplitBlock) {
+        const int nb = min(kEpiSplitBlock, p.splits - sp0);
+        const int vals = nb * cols;
+#pragma unroll 8
+        for (int i = tid; i < vals; i += kEpiThreads) {
+            const int sp = i / cols;
+            const int j = i - sp * cols;
+            sPart[i] = __ldcg(p.partials + (static_cast<int64_t>(sp0 + sp) * p.M + r) * p.W + j);
         }
-        if (tid < mix) sMix[tid] = acc; else sSum = acc;
+        __syncthreads();
+        if (tid < cols)
+            for (int sp = 0; sp < nb; ++sp) acc = __fadd_rn(acc, sPart[sp * cols + tid]);
+        __syncthreads();
     }
+    if (tid < mix) sMix[tid] = acc;
+    else if (tid == mix) sSum = acc;
     __syncthreads();
     // invRms = 1 / Sqrt(sum * invFlatDim + normEps)   (mhc_pre.cpp:504-519)
     float v = __fmul_rn(sSum, p.invK);
@@ -546,12 +569,32 @@ int launch_prepare(const Problem& p, const Plan& plan, const float* phi, const f
     return cudaGetLastError();
 }
 
+// Raises a kernel's dynamic shared memory limit on the current device when the
+// launch needs more than was already set there (the attribute call costs host time,
+// so each kernel remembers the largest value set per device).
+constexpr int kMaxDevices = 64;
+template <typename Kern>
+static cudaError_t ensure_smem(Kern kern, std::atomic<int> (&setBytes)[kMaxDevices], size_t bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const int want = static_cast<int>(bytes);
+    if (dev >= 0 && dev < kMaxDevices && setBytes[dev].load(std::memory_order_acquire) >= want) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+        int cur = setBytes[dev].load(std::memory_order_relaxed);
+        while (cur < want && !setBytes[dev].compare_exchange_weak(cur, want, std::memory_order_release)) {
+        }
+    }
+    return e;
+}
+
 template <int DT, int N>
 static int launch_gemm(const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap, const GemmParams& gp,
                        cudaStream_t stream) {
     auto kern = gemm_sumsq_kernel<DT, N>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(plan.smemBytes));
+    static std::atomic<int> setBytes[kMaxDevices];
+    cudaError_t e = ensure_smem(kern, setBytes, plan.smemBytes);
     if (e != cudaSuccess) return e;
     kern<<<plan.gemmGrid, kGemmThreads, plan.smemBytes, stream>>>(xMap, phiMap, gp);
     return cudaGetLastError();
@@ -559,16 +602,27 @@ static int launch_gemm(const Plan& plan, const CUtensorMap& xMap, const CUtensor
 
 template <int DT, int NS>
 static int launch_epi(const Problem& p, const EpiParams& ep, cudaStream_t stream) {
-    epilogue_hin_kernel<DT, NS><<<static_cast<unsigned>(p.M), kEpiThreads, 0, stream>>>(ep);
-    return cudaGetLastError();
+    const size_t smem = static_cast<size_t>(std::min(ep.splits, kEpiSplitBlock)) * (p.mix + 1) * sizeof(float);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.M), 1, 1);
+    cfg.blockDim = dim3(kEpiThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    // programmatic dependent launch: starts while the GEMM drains, waits in-kernel
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, epilogue_hin_kernel<DT, NS>, ep);
 }
 
 template <int DT, int NS>
 static int launch_fused_t(const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap, const FusedParams& fp,
                           cudaStream_t stream) {
     auto kern = mhc_pre_fused_kernel<DT, NS>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(plan.smemBytes));
+    static std::atomic<int> setBytes[kMaxDevices];
+    cudaError_t e = ensure_smem(kern, setBytes, plan.smemBytes);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(plan.teams * plan.teamS), 1, 1);

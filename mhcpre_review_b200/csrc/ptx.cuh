@@ -104,6 +104,24 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* m
         : "memory");
 }
 
+// Plain bulk copy global -> shared (no tensor map, no multicast): both addresses and
+// the size are multiples of 16 bytes.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Programmatic dependent launch: the dependent grid may start launching once every
+// CTA of this grid has called launch_dependents (or exited); wait blocks until the
+// grids this one depends on have completed and their memory is visible.
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Orders this thread's generic-proxy accesses against its async-proxy (TMA/bulk) ones.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
