@@ -156,10 +156,11 @@ MHC_API int mhcPreRunNoAlloc(const mhcPreDesc_t* desc, const void* x, const floa
 /* Execution plan chosen for a description on the current device (for tests,
  * benchmarks and profiling; no reference counterpart). */
 typedef struct {
-    int32_t path;           /* 0 = split-K GEMM + epilogue kernels, 1 = fused single kernel */
+    int32_t path;           /* 0 = split-K GEMM + epilogue kernels, 1 = fused team kernel
+                               (opt-in), 2 = single-launch decode kernel (M <= 32) */
     int32_t kernelsPerRun;  /* kernels launched by mhcPreRunPrepared */
     int32_t gridCtas;       /* CTAs of the main kernel */
-    int32_t splits;         /* K splits (path 0) or team size (path 1) */
+    int32_t splits;         /* K splits (paths 0 and 2) or team size (path 1) */
     int32_t rowsPerTile;    /* token rows per tensor-core tile */
     int32_t reserved[3];
 } mhcPrePlan_t;

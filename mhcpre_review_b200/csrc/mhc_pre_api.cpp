@@ -100,6 +100,26 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     pl.partBytes = static_cast<size_t>(splits) * static_cast<size_t>(p.M) * static_cast<size_t>(p.W) * 4;
     pl.totalBytes = align_up(pl.partOffset + pl.partBytes, 256);
 
+    // Path 2, the decode kernel, for M up to kDecodeMaxRows: one cooperative launch
+    // of one CTA per SM (at most one per 64-wide chunk), CUDA-core partial sums per
+    // K-slice, a grid barrier, then the per-row reduction, epilogue and hIn.
+    // MHC_PRE_PATH=0 or =1 in the environment turns it off (tests, tuning).
+    {
+        const char* fp = std::getenv("MHC_PRE_PATH");
+        if (p.M <= kDecodeMaxRows && (fp == nullptr || fp[0] == '2')) {
+            pl.path = 2;
+            pl.splits = std::min(smCount, pl.chunks);
+            pl.gemmGrid = pl.splits;
+            pl.stages = 0;
+            pl.smemBytes = decode_smem(p);
+            pl.partOffset = align_up(pl.phiOffset + pl.phiBytes, 256);
+            pl.partBytes = static_cast<size_t>(pl.splits) * static_cast<size_t>(p.M) * static_cast<size_t>(p.W) * 4;
+            pl.totalBytes = align_up(pl.partOffset + pl.partBytes, 256);
+            *plan = pl;
+            return MHC_STATUS_SUCCESS;
+        }
+    }
+
     // Path 1, the fused kernel, when D splits into 64-wide chunks evenly over a team
     // (a row's arithmetic depends on the team size S only, not on M).  S divides
     // D/64.  Its hIn pass re-reads x from L2, which can hit only while the tiles the
@@ -240,9 +260,14 @@ static int run_prepared(const Problem& p, const Plan& plan, const void* x, const
     if (!aligned16(x) || !aligned16(hIn) || !aligned4(hPost) || !aligned4(hRes) || !aligned4(alpha) ||
         !aligned4(bias))
         return MHC_STATUS_MISALIGNED;
+    CUtensorMap xMap{}, phiMap{};
+    if (plan.path == 2) {  // the decode kernel reads with plain loads: no tensor maps
+        const int e = launch_run(p, plan, xMap, phiMap, x, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin,
+                                 evEnd);
+        return e == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
+    }
     EncodeTiledFn enc = get_encode_fn();
     if (enc == nullptr) return MHC_STATUS_CUDA_ERROR;
-    CUtensorMap xMap, phiMap;
     int rc = encode_2d(enc, &xMap, x, p.dtype, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), kRowsPerTile);
     if (rc != 0) return rc;
     const void* phiPrep = static_cast<const uint8_t*>(workspace) + plan.phiOffset;
@@ -331,7 +356,7 @@ int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* out) {
     if (rc != 0) return rc;
     std::memset(out, 0, sizeof(*out));
     out->path = plan.path;
-    out->kernelsPerRun = plan.path == 1 ? 1 : 2;
+    out->kernelsPerRun = plan.path == 0 ? 2 : 1;
     out->gridCtas = plan.path == 1 ? plan.teams * plan.teamS : plan.gemmGrid;
     out->splits = plan.path == 1 ? plan.teamS : plan.splits;
     out->rowsPerTile = kRowsPerTile;

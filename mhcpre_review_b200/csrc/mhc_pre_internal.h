@@ -16,7 +16,12 @@ struct WorkspaceHeader {
     uint32_t magic;       // kPreparedMagic once weights are prepared
     int32_t phiScaleExp;  // fp16: prepared phi' = phi * 2^exp (bf16: 0)
     uint32_t signature;   // hash of the description the weights were prepared for
-    uint32_t pad[61];     // pad[0]: max |phi'| bits during preparation
+    uint32_t maxAbsBits;  // max |phi'| (float bits) during preparation
+    // Arrivals at the decode kernel's grid barrier, summed over all its launches on
+    // this workspace (zeroed with the header when weights are prepared); every
+    // launch adds exactly its grid size.
+    unsigned long long gridBarrier;
+    uint32_t pad[58];
 };
 static_assert(sizeof(WorkspaceHeader) == 256, "header is 256 bytes");
 constexpr uint32_t kPreparedMagic = 0x5048434Du;  // "MCHP"
@@ -25,6 +30,7 @@ constexpr int kRowsPerTile = 128;  // token rows per tensor-core tile (MMA M)
 constexpr int kChunk = 64;         // K elements per TMA box / pipeline stage (128 bytes)
 constexpr int kMaxMix = 80;
 constexpr int kFusedSlots = 2;     // record/hPre slots per team in the fused kernel
+constexpr int kDecodeMaxRows = 32; // M up to this runs the single-launch decode kernel
 
 // Everything a launch needs, derived once from the description.
 struct Problem {
@@ -43,7 +49,7 @@ struct Problem {
 };
 
 struct Plan {
-    int path;        // 0: split-K GEMM + epilogue kernels, 1: fused team kernel
+    int path;        // 0: split-K GEMM + epilogue kernels, 1: fused team kernel, 2: decode kernel
     int tilesM;      // ceil(M / 128)
     int chunks;      // ceil(K / 64)
     int splits;      // K splits (path 0)
@@ -68,6 +74,7 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
                const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
                void* workspace, cudaStream_t stream, cudaEvent_t evBegin = nullptr, cudaEvent_t evEnd = nullptr);
 int read_and_clear_device_status(int32_t* status);
+size_t decode_smem(const Problem& p);  // dynamic shared memory of the decode kernel
 
 // Validation + plan for the current device, and prepare-then-run into a given
 // workspace (used by the no-allocation entry point).

@@ -82,7 +82,7 @@ __global__ void prep_split_kernel(const float* __restrict__ phi, const float* __
     int e = 0;
     if constexpr (DT == MHC_DTYPE_F16) {
         // Scale so that max|phi'| * 2^e < 2^15: hi and lo then stay normal fp16.
-        const float mx = __uint_as_float(hdr->pad[0]);
+        const float mx = __uint_as_float(hdr->maxAbsBits);
         if (mx > 0.0f) {
             int ex = 0;
             frexpf(mx, &ex);
@@ -546,6 +546,7 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
 }
 
 #include "mhc_pre_fused.cuh"
+#include "mhc_pre_decode.cuh"
 
 // ---------------------------------------------------------------------------
 // Launchers
@@ -561,7 +562,7 @@ int launch_prepare(const Problem& p, const Plan& plan, const float* phi, const f
     const int threads = 256;
     const int blocks = static_cast<int>(std::min<int64_t>((total + threads - 1) / threads, 148 * 8));
     if (p.dtype == MHC_DTYPE_F16) {
-        prep_maxabs_kernel<<<blocks, threads, 0, stream>>>(phi, g, p.K, p.mix, &hdr->pad[0]);
+        prep_maxabs_kernel<<<blocks, threads, 0, stream>>>(phi, g, p.K, p.mix, &hdr->maxAbsBits);
         prep_split_kernel<MHC_DTYPE_F16><<<blocks, threads, 0, stream>>>(phi, g, p.K, p.mix, hdr, out, p.signature);
     } else {
         prep_split_kernel<MHC_DTYPE_BF16><<<blocks, threads, 0, stream>>>(phi, g, p.K, p.mix, hdr, out, p.signature);
@@ -685,11 +686,73 @@ static int launch_fused(const Problem& p, const Plan& plan, const CUtensorMap& x
     return 0;
 }
 
+template <int DT, int NS>
+static int launch_decode_t(const Plan& plan, const DecodeParams& dp, cudaStream_t stream) {
+    auto kern = mhc_pre_decode_kernel<DT, NS>;
+    static std::atomic<int> setBytes[kMaxDevices];
+    cudaError_t e = ensure_smem(kern, setBytes, plan.smemBytes);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.gemmGrid), 1, 1);
+    cfg.blockDim = dim3(kDecodeThreads, 1, 1);
+    cfg.dynamicSmemBytes = plan.smemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // the grid barrier needs every CTA resident
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, dp);
+}
+
+static int launch_decode(const Problem& p, const Plan& plan, const void* x, const float* alpha, const float* bias,
+                         void* hIn, float* hPost, float* hRes, void* workspace, cudaStream_t stream,
+                         cudaEvent_t evBegin, cudaEvent_t evEnd) {
+    auto* hdr = reinterpret_cast<WorkspaceHeader*>(workspace);
+    DecodeParams dp;
+    dp.M = static_cast<int>(p.M);
+    dp.chunks = plan.chunks;
+    dp.W = p.W;
+    dp.K = p.K;
+    dp.D = p.D;
+    dp.invK = 1.0f / static_cast<float>(p.K);
+    dp.normEps = p.normEps;
+    dp.hcEps = p.hcEps;
+    dp.x = static_cast<const uint16_t*>(x);
+    dp.phi = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(workspace) + plan.phiOffset);
+    dp.alpha = alpha;
+    dp.bias = bias;
+    dp.hIn = static_cast<uint16_t*>(hIn);
+    dp.hPost = hPost;
+    dp.hRes = hRes;
+    dp.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.partOffset);
+    dp.barrier = &hdr->gridBarrier;
+    dp.hdr = hdr;
+    if (evBegin != nullptr && cudaEventRecord(evBegin, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    const bool bf = p.dtype == MHC_DTYPE_BF16;
+    int rc;
+    switch (p.n) {
+        case 4: rc = bf ? launch_decode_t<MHC_DTYPE_BF16, 4>(plan, dp, stream)
+                        : launch_decode_t<MHC_DTYPE_F16, 4>(plan, dp, stream); break;
+        case 6: rc = bf ? launch_decode_t<MHC_DTYPE_BF16, 6>(plan, dp, stream)
+                        : launch_decode_t<MHC_DTYPE_F16, 6>(plan, dp, stream); break;
+        default: rc = bf ? launch_decode_t<MHC_DTYPE_BF16, 8>(plan, dp, stream)
+                         : launch_decode_t<MHC_DTYPE_F16, 8>(plan, dp, stream); break;
+    }
+    if (rc != 0) return rc;
+    if (evEnd != nullptr && cudaEventRecord(evEnd, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    return 0;
+}
+
+size_t decode_smem(const Problem& p) { return decode_smem_bytes(static_cast<int>(p.M), p.mix); }
+
 int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
                const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
                void* workspace, cudaStream_t stream, cudaEvent_t evBegin, cudaEvent_t evEnd) {
     if (plan.path == 1)
         return launch_fused(p, plan, xMap, phiMap, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
+    if (plan.path == 2)
+        return launch_decode(p, plan, x, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
     GemmParams gp;
     gp.M = p.M;
     gp.tilesM = plan.tilesM;
