@@ -4,11 +4,12 @@
 
 A step is one MhcPre call over one batch of the workload (default: BASELINE
 config 4, M = 65536 tokens (B=16, S=4096), n=4, D=7168, bf16, gamma on) with the
-weights prepared once beforehand (they are model parameters).  Each GPU processes
-its own batch of that size (token sharding, phi replicated, no collective on the
-data path), so scaling is weak; value = tokens all ranks processed / the slowest
-rank's device time.  Inputs (3.76 GB of x per GPU) are larger than the 126 MB L2,
-so no flush is needed between steps.
+weights prepared once beforehand (they are model parameters).  With N GPUs the
+batch's tokens are sharded: rank r takes the contiguous rows shard_range(M, N, r)
+(phi replicated, no collective on the data path), so the total work is fixed and
+scaling is strong; value = M / the slowest rank's device time.  Inputs (3.76 GB of
+x on one GPU, 0.47 GB per GPU at N=8) are larger than the 126 MB L2, so no flush
+is needed between steps.
 
 The JSON line also carries:
   roofline      the main kernel's algorithmic bytes per launch / its average launch
@@ -91,6 +92,15 @@ def committed_traffic(kernel: str, workload: str):
         return d.get(kernel, {}).get(workload)
     except Exception:
         return None
+
+
+def scaled_traffic(traffic, rows, total):
+    """DRAM bytes per launch from the committed ncu summary (captured on the full
+    one-GPU workload), scaled to a shard's rows: the GEMM's traffic is x plus the
+    prepared weights, in proportion to the rows."""
+    if traffic is None:
+        return None
+    return int(traffic * rows / total)
 
 
 class ClockSampler:
@@ -202,11 +212,13 @@ def cpu_sample_rows(cfg, x, phi, alpha, bias, gamma, threads, target_s=10.0):
 
 
 def workload_config(cfg, n_gpus):
-    return {"workload": f"{cfg.name}: M={cfg.M} (B={cfg.batch},S={cfg.seq}) per GPU, n={cfg.n}, D={cfg.D}, "
+    from mhcpre_review_b200.shard import shard_range
+    rows = shard_range(cfg.M, n_gpus, 0)[1]
+    return {"workload": f"{cfg.name}: M={cfg.M} (B={cfg.batch},S={cfg.seq}) in total, n={cfg.n}, D={cfg.D}, "
                         f"{cfg.dtype}, gamma {'on' if cfg.gamma else 'off'}",
-            "tokens_per_gpu": cfg.M, "global_tokens": cfg.M * n_gpus, "streams": cfg.n, "head_dim": cfg.D,
-            "parallelism": f"token-sharded x{n_gpus}, phi replicated, no collective",
-            "l2": "inputs larger than L2 (x = %.2f GB per GPU), no flush" % (cfg.M * cfg.K * 2 / 1e9)}
+            "tokens_per_gpu": rows, "global_tokens": cfg.M, "streams": cfg.n, "head_dim": cfg.D,
+            "parallelism": f"token-sharded x{n_gpus} (contiguous rows), phi replicated, no collective",
+            "l2": "inputs larger than L2 (x = %.2f GB per GPU), no flush" % (rows * cfg.K * 2 / 1e9)}
 
 
 def run_reference(args, cfg, world, rank):
@@ -225,7 +237,7 @@ def run_reference(args, cfg, world, rank):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3 * cfg.M / rows,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": cfg.dtype,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": cfg.dtype,
         "data": "synthetic (seeded, BASELINE config shapes and distributions)",
         "config": workload_config(cfg, args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
@@ -236,7 +248,7 @@ def run_reference(args, cfg, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def measure_e2e(mp, inp, cfg, steps, pg, dist, world):
+def measure_e2e(mp, inp, cfg, steps, pg, dist, world, total_tokens):
     """Public API with pinned host buffers: H2D x, run, D2H outputs, per step,
     chunked over rows on three streams so the copies overlap the kernels."""
     import torch
@@ -299,7 +311,7 @@ def measure_e2e(mp, inp, cfg, steps, pg, dist, world):
     if pg:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    return {"value": world * cfg.M / (ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+    return {"value": total_tokens / (ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms, "chunks": chunks, "pinned_host": True}
 
 
@@ -388,11 +400,16 @@ def main():
     import mhcpre_review_b200 as mp
     from mhcpre_review_b200.configs import make_inputs, with_shape
 
-    # each rank: its own batch (x seed offset by rank), weights identical on all ranks
-    inp = make_inputs(with_shape(cfg, seed=cfg.seed + 1000 * rank) if rank else cfg)
-    if rank:
-        w = make_inputs(with_shape(cfg, batch=1, seq=1))  # same weight seeds as rank 0
-        inp.update(phi=w["phi"], gamma=w["gamma"], alpha=w["alpha"], bias=w["bias"])
+    # every rank generates the same batch (same seeds) and keeps its contiguous rows;
+    # the weights are replicated
+    from mhcpre_review_b200.shard import shard_range
+    total = cfg.M
+    start, rows = shard_range(total, world, rank)
+    inp = make_inputs(cfg)
+    inp["x"] = inp["x"].reshape(total, cfg.n, cfg.D)[start:start + rows].reshape(1, rows, cfg.n, cfg.D).clone()
+    torch.cuda.empty_cache()
+    full_cfg = cfg
+    cfg = with_shape(cfg, batch=1, seq=rows)  # this rank's shard
     x = inp["x"]
     ex = mp.MhcPre(cfg.batch, cfg.seq, cfg.n, cfg.D, x.dtype, cfg.gamma, cfg.norm_eps, cfg.hc_eps)
     ex.prepare(inp["phi"], inp["gamma"])
@@ -433,7 +450,7 @@ def main():
     if pg:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_step = float(t.item()) / args.steps
-    value = world * cfg.M / (ms_step * 1e-3)
+    value = total / (ms_step * 1e-3)
 
     # roofline of the main kernel
     peak, peak_kind = measured_peaks()
@@ -447,14 +464,15 @@ def main():
     op_gbs = cfg.algorithmic_bytes() / (ms_step * 1e-3) / 1e9
     roofline = {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                "traffic": committed_traffic(kernel, cfg.name), "algorithmic_bytes_per_launch": kbytes,
+                "traffic": scaled_traffic(committed_traffic(kernel, cfg.name), rows, total),
+                "algorithmic_bytes_per_launch": kbytes,
                 "launch_ms": main_avg_ms, "op_GBps": op_gbs, "op_frac_of_8TBps": op_gbs / 8000.0}
 
     e2e = None
     if not args.no_e2e:
         del out
         torch.cuda.empty_cache()
-        e2e = measure_e2e(mp, inp, cfg, args.e2e_steps, pg, dist, world)
+        e2e = measure_e2e(mp, inp, cfg, args.e2e_steps, pg, dist, world, total)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -468,10 +486,11 @@ def main():
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": cfg.dtype,
             "data": "synthetic (seeded, BASELINE config shapes and distributions)",
-            "config": workload_config(cfg, world), "plan": plan, "gpu_launches": args.steps * plan["kernels_per_run"],
+            "config": workload_config(full_cfg, world), "plan": plan,
+            "gpu_launches": args.steps * plan["kernels_per_run"],
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -80,7 +80,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
 }
 
 // ---------------------------------------------------------------------------
-// TMA (bulk tensor copies global -> shared), no multicast.
+// TMA (bulk tensor copies global -> this CTA's shared memory).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -104,7 +104,7 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* m
         : "memory");
 }
 
-// Plain bulk copy global -> shared (no tensor map, no multicast): both addresses and
+// Plain bulk copy global -> this CTA's shared memory (no tensor map): both addresses and
 // the size are multiples of 16 bytes.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
