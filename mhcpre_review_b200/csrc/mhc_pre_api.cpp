@@ -74,6 +74,8 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     int splits = groups;
     if (p.M < kShardRows && pl.tilesM < smCount)
         splits = std::max(groups, std::min(smCount / pl.tilesM, std::max(1, pl.chunks / kMinSplitChunks)));
+    // Tuning override: MHC_PRE_SPLITS (K splits of the split-K path).
+    if (const char* sp = std::getenv("MHC_PRE_SPLITS")) splits = std::max(1, std::atoi(sp));
     splits = std::min(splits, pl.chunks);
     pl.splits = splits;
     pl.gemmGrid = std::min(pl.tilesM * splits, smCount);

@@ -59,49 +59,6 @@ constexpr int kFusedThreads = 384;  // 12 warps
 constexpr int kSlots = kFusedSlots;
 constexpr int kHinStageBytes = kRowsPerTile * kChunk * 2;  // 16 KB
 
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Polls *ctr until it reaches target (acquire).  Bounded; also gives up when the
-// team-wide abort word is set.
-__device__ __forceinline__ bool wait_counter(const unsigned* ctr, unsigned target, const unsigned* gabort) {
-    if (ld_acquire_u32(ctr) >= target) return true;
-    const uint64_t t0 = global_timer_ns();
-    for (uint32_t i = 0; i < kMaxPolls; ++i) {
-        if (ld_acquire_u32(ctr) >= target) return true;
-        if ((i & 63u) == 63u) {
-            if (*reinterpret_cast<const volatile unsigned*>(gabort) != 0) return false;
-            if (global_timer_ns() - t0 > kWaitLimitNs) return false;
-        }
-        __nanosleep(64);
-    }
-    return false;
-}
-
-// Barrier among `nthreads` threads on named barrier `id` that also ORs a predicate
-// across them (every participant gets the same answer).
-__device__ __forceinline__ bool bar_red_or(uint32_t id, uint32_t nthreads, bool pred) {
-    uint32_t r;
-    asm volatile(
-        "{\n"
-        ".reg .pred p, q;\n"
-        "setp.ne.u32 p, %3, 0;\n"
-        "bar.red.or.pred q, %1, %2, p;\n"
-        "selp.u32 %0, 1, 0, q;\n"
-        "}\n"
-        : "=r"(r)
-        : "r"(id), "r"(nthreads), "r"(pred ? 1u : 0u)
-        : "memory");
-    return r != 0;
-}
-
 template <int N>
 struct FusedCfg {
     static constexpr int kXBytes = kRowsPerTile * kChunk * 2;
