@@ -457,6 +457,8 @@ def main():
     main_avg_ms = sum(main_ms) / len(main_ms)
     if plan["path"] == 1:
         kernel, kbytes = "mhc_pre_fused", cfg.algorithmic_bytes()
+    elif plan["path"] == 2:
+        kernel, kbytes = "mhc_pre_decode", cfg.algorithmic_bytes()
     else:
         kernel = "gemm_sumsq"
         kbytes = cfg.M * cfg.K * 2 + 4 * cfg.K * cfg.mix + (4 * cfg.K if cfg.gamma else 0)
