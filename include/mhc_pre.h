@@ -172,6 +172,16 @@ MHC_API int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* plan);
  * *deviceStatus receives 0 or a negative mhcStatus_t. */
 MHC_API int mhcPreGetDeviceStatus(int32_t* deviceStatus);
 
+/* Diagnostics for failure detection: launches one kernel that waits, with a limit
+ * of limitMicroseconds (1 .. 1e6), on a global counter that nothing increments and
+ * on an mbarrier that nothing arrives on -- the two kinds of bounded wait the
+ * kernels use.  Both waits give up; the kernel sets the device status word to
+ * MHC_STATUS_DEVICE_TIMEOUT (read it with mhcPreGetDeviceStatus) and returns
+ * normally, leaving the context usable.  *countersGaveUp / *barriersGaveUp receive
+ * 1 where the wait gave up.  Synchronizes the stream.  No reference counterpart. */
+MHC_API int mhcPreDiagWaitTimeout(uint32_t limitMicroseconds, int32_t* countersGaveUp, int32_t* barriersGaveUp,
+                                  void* stream);
+
 /* Human-readable name of a status code (static string). */
 MHC_API const char* mhcPreStatusString(int status);
 

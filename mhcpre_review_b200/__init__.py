@@ -34,7 +34,7 @@ STATUS_NAMES = {
 EXPORTED_SYMBOLS = (
     "mhcPreGetWorkspaceSize", "mhcPrePrepareWeights", "mhcPreRun", "mhcPreRunPrepared",
     "mhcPreRunPreparedProfiled", "mhcPreQueryPlan", "mhcPreGetDeviceStatus", "mhcPreStatusString",
-    "mhcPreAbiVersion", "mhcPreRunNoAlloc",
+    "mhcPreAbiVersion", "mhcPreRunNoAlloc", "mhcPreDiagWaitTimeout",
 )
 
 
@@ -120,6 +120,16 @@ def device_status() -> int:
     s = ctypes.c_int32(0)
     _check(lib().mhcPreGetDeviceStatus(ctypes.byref(s)), "GetDeviceStatus")
     return int(s.value)
+
+
+def diag_wait_timeout(limit_us: int = 2000, stream=None) -> tuple[bool, bool]:
+    """Makes a counter wait and an mbarrier wait run out on the device (nothing ever
+    signals them) with the given limit; returns (counter gave up, barrier gave up).
+    The device status word is left at MHC_STATUS_DEVICE_TIMEOUT."""
+    c, b = ctypes.c_int32(0), ctypes.c_int32(0)
+    _check(lib().mhcPreDiagWaitTimeout(ctypes.c_uint32(limit_us), ctypes.byref(c), ctypes.byref(b),
+                                       _stream_ptr(stream)), "DiagWaitTimeout")
+    return bool(c.value), bool(b.value)
 
 
 def _torch():

@@ -406,6 +406,23 @@ int mhcPreRun(const mhcPreDesc_t* desc, const void* x, const float* phi, const f
     return mhcPreRunPrepared(desc, x, alpha, bias, hIn, hPost, hRes, workspace, workspaceBytes, stream);
 }
 
+int mhcPreDiagWaitTimeout(uint32_t limitMicroseconds, int32_t* countersGaveUp, int32_t* barriersGaveUp,
+                          void* stream) {
+    if (countersGaveUp == nullptr || barriersGaveUp == nullptr) return MHC_STATUS_NULL_POINTER;
+    if (limitMicroseconds == 0 || limitMicroseconds > 1000000u) return MHC_STATUS_BAD_SHAPE;
+    int major = 0, dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+        return MHC_STATUS_CUDA_ERROR;
+    if (major != 10) return MHC_STATUS_UNSUPPORTED_DEVICE;
+    int r[2] = {0, 0};
+    if (diag_wait_timeout(static_cast<uint64_t>(limitMicroseconds) * 1000u, r, static_cast<cudaStream_t>(stream)) != 0)
+        return MHC_STATUS_CUDA_ERROR;
+    *countersGaveUp = r[0];
+    *barriersGaveUp = r[1];
+    return MHC_STATUS_SUCCESS;
+}
+
 int mhcPreGetDeviceStatus(int32_t* deviceStatus) {
     if (deviceStatus == nullptr) return MHC_STATUS_NULL_POINTER;
     const int e = read_and_clear_device_status(deviceStatus);

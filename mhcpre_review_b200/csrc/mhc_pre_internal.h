@@ -75,6 +75,7 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
                void* workspace, cudaStream_t stream, cudaEvent_t evBegin = nullptr, cudaEvent_t evEnd = nullptr);
 int read_and_clear_device_status(int32_t* status);
 size_t decode_smem(const Problem& p);  // dynamic shared memory of the decode kernel
+int diag_wait_timeout(uint64_t limit_ns, int* result_host, cudaStream_t stream);
 
 // Validation + plan for the current device, and prepare-then-run into a given
 // workspace (used by the no-allocation entry point).

@@ -804,6 +804,45 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
     }
 }
 
+// ---------------------------------------------------------------------------
+// Diagnostics: the bounded waits give up as designed
+// ---------------------------------------------------------------------------
+// A counter that nothing ever sets.
+__device__ unsigned g_diag_never_set = 0;
+
+// Waits, with the given limit, on the two kinds of wait the kernels use: a global
+// counter (cross-CTA handshakes) that nothing increments, and an mbarrier (TMA and
+// MMA rings) that nothing arrives on.  Both must give up; the kernel then reports
+// MHC_STATUS_DEVICE_TIMEOUT through the device status word and returns normally,
+// so the context stays usable.  result[0..1] = 1 where a wait gave up.
+__global__ void diag_wait_timeout_kernel(uint64_t limit_ns, int* result) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbarrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool counterDone = wait_counter(&g_diag_never_set, 1u, nullptr, limit_ns);
+        const bool barrierDone = mbar_wait(&bar, 0u, nullptr, limit_ns);
+        result[0] = counterDone ? 0 : 1;
+        result[1] = barrierDone ? 0 : 1;
+        if (!counterDone || !barrierDone) set_device_status(MHC_STATUS_DEVICE_TIMEOUT);
+    }
+}
+
+int diag_wait_timeout(uint64_t limit_ns, int* result_host, cudaStream_t stream) {
+    int* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, 2 * sizeof(int));
+    if (e != cudaSuccess) return e;
+    diag_wait_timeout_kernel<<<1, 32, 0, stream>>>(limit_ns, d);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(result_host, d, 2 * sizeof(int), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    cudaFree(d);
+    return e;
+}
+
 int read_and_clear_device_status(int32_t* status) {
     int v = 0;
     cudaError_t e = cudaDeviceSynchronize();

@@ -261,14 +261,15 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
 // Cross-CTA signalling through global memory: a release add by the producer, an
 // acquire poll by the consumer.  Polls *ctr until it reaches target.  Bounded;
 // also gives up when *gabort (a global abort word, may be null) becomes non-zero.
-__device__ __forceinline__ bool wait_counter(const unsigned* ctr, unsigned target, const unsigned* gabort) {
+__device__ __forceinline__ bool wait_counter(const unsigned* ctr, unsigned target, const unsigned* gabort,
+                                             uint64_t limit_ns = kWaitLimitNs) {
     if (ld_acquire_u32(ctr) >= target) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 0; i < kMaxPolls; ++i) {
         if (ld_acquire_u32(ctr) >= target) return true;
         if ((i & 63u) == 63u) {
             if (gabort != nullptr && *reinterpret_cast<const volatile unsigned*>(gabort) != 0) return false;
-            if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+            if (global_timer_ns() - t0 > limit_ns) return false;
         }
         __nanosleep(64);
     }
