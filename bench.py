@@ -481,9 +481,15 @@ def main():
         xb, phi, alpha, bias, gamma = host_inputs(cfg)
         threads = cpu_cores()
         rows = cpu_sample_rows(cfg, xb, phi, alpha, bias, gamma, threads, target_s=10.0)
-        secs = time_oracle(cfg, xb, phi, alpha, bias, gamma, rows, threads)
-        cpu = {"value": rows / secs, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"first {rows} of the {cfg.M} rows of {cfg.name} (same inputs), one pass, {secs:.1f} s"}
+        # repeat the sample until about 10 s of CPU work (the whole workload can be
+        # faster than that on many cores)
+        secs, passes = 0.0, 0
+        while passes < 1 or (secs < 10.0 and passes < 50):
+            secs += time_oracle(cfg, xb, phi, alpha, bias, gamma, rows, threads)
+            passes += 1
+        cpu = {"value": rows * passes / secs, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"first {rows} of the {cfg.M} rows of {cfg.name} (same inputs), {passes} pass(es), "
+                         f"{secs:.1f} s"}
 
     if rank == 0:
         line = {

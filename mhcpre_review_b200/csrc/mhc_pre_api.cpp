@@ -82,13 +82,21 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     const size_t stageBytes = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + static_cast<size_t>(p.N) * kChunk * 2;
     const size_t smemLimit = 232448;  // sm_100 per-block opt-in maximum
     const size_t fixed = 1024 /*alignment slack*/ + 256 /*barriers*/;
-    // Two GEMM CTAs per SM when their TMEM (3 accumulator buffers of N columns,
-    // rounded to a power of two) fits twice: a single CTA's MMA stream leaves the
-    // tensor core idle between its dependent steps, two interleave.
-    const int accCols = 3 * p.N <= 64 ? 64 : 3 * p.N <= 128 ? 128 : 3 * p.N <= 256 ? 256 : 512;
-    int ctasPerSm = accCols <= 256 ? 2 : 1;
-    if (const char* ct = std::getenv("MHC_PRE_GEMM_CTAS")) ctasPerSm = std::max(1, std::min(std::atoi(ct), 512 / accCols));
-    const size_t budget = ctasPerSm == 1 ? smemLimit : 110 * 1024;
+    // GEMM CTAs per SM.  One CTA's MMA issue stream retires a tcgen05.mma about every
+    // 145 cycles whatever N is, and a CTA's ring holds only so many bytes in flight,
+    // so more CTAs per SM stream faster, as far as TMEM (two accumulator buffers of N
+    // columns, rounded to a power of two) and registers allow: three for n=4 (the
+    // kernel is compiled for three), two for n=6, one for n=8.  Three CTAs (3 stages
+    // each) pay off when the items fill at least six rounds of them; with fewer, the
+    // 4-stage rings of two CTAs lose less to the last round.
+    const int accCols = 2 * p.N <= 64 ? 64 : 2 * p.N <= 128 ? 128 : 2 * p.N <= 256 ? 256 : 512;
+    const int maxCtas = std::min(512 / accCols, p.N <= 48 ? 3 : 2);
+    const int64_t items = static_cast<int64_t>(pl.tilesM) * splits;
+    int ctasPerSm = maxCtas;
+    if (ctasPerSm == 3 && items < 6 * 3 * static_cast<int64_t>(smCount)) ctasPerSm = 2;
+    // Tuning override: MHC_PRE_GEMM_CTAS (CTAs per SM, within the limits above).
+    if (const char* ct = std::getenv("MHC_PRE_GEMM_CTAS")) ctasPerSm = std::max(1, std::min(std::atoi(ct), maxCtas));
+    const size_t budget = ctasPerSm == 1 ? smemLimit : ctasPerSm == 2 ? 110 * 1024 : 74 * 1024;
     int stages = static_cast<int>((budget - fixed) / stageBytes);
     stages = std::max(2, std::min(stages, 8));
     // Tuning override: MHC_PRE_GEMM_STAGES (ring depth).

@@ -51,6 +51,7 @@ struct DecodeParams {
     float* part;                     // [G][M][W]
     unsigned long long* barrier;     // WorkspaceHeader::gridBarrier
     const WorkspaceHeader* hdr;
+    uint32_t signature;              // of the description (checked against the prepared weights)
 };
 
 // Shared memory of the decode kernel, in bytes (host and device agree on it).
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) mhc_pre_decode_kernel(const
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const int M = p.M;
-    const bool prepared = p.hdr->magic == kPreparedMagic;
+    const bool prepared = p.hdr->magic == kPreparedMagic && p.hdr->signature == p.signature;
 
     // ---------------- phase 1: partial records of this CTA's K-slice ----------------
     const int c0 = static_cast<int>(static_cast<int64_t>(g) * p.chunks / G);

@@ -51,6 +51,7 @@ struct FusedParams {
     float* hpre;     // [T][2][128][8]
     unsigned* cnt;   // [T][2*kSlots]: record arrivals per slot, then hPre arrivals per slot; [2*kSlots*T]: abort word
     const WorkspaceHeader* hdr;
+    uint32_t signature;  // of the description (checked against the prepared weights)
 };
 
 constexpr int kFusedThreads = 384;  // 12 warps
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tacc = *tmemSlot;
-    const bool prepared = p.hdr->magic == kPreparedMagic;
+    const bool prepared = p.hdr->magic == kPreparedMagic && p.hdr->signature == p.signature;
     if (!prepared && threadIdx.x == 0) set_device_status(MHC_STATUS_NOT_PREPARED);
 
     auto fail = [&]() {

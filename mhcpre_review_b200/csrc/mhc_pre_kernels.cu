@@ -129,6 +129,7 @@ struct GemmParams {
     int chunks;
     int splits;
     int stages;
+    uint32_t signature;  // of the description: the workspace must hold weights prepared for it
     float* partials;
     const WorkspaceHeader* hdr;
 };
@@ -166,10 +167,15 @@ constexpr int kGemmThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 square-s
 // K chunks; finished segments are added into IEEE fp32 registers by the epilogue
 // warps while the MMA fills the other accumulator buffer.
 constexpr int kSegChunks = 4;
-// Accumulator buffers: the square-sum warps add segment s-2 into registers while the
-// MMA fills segment s, so they never wait for the tensor core to finish.
-constexpr int kAccBufs = 3;
+// Accumulator buffers: the square-sum warps add segment s-1 into registers while the
+// MMA fills segment s.  Two buffers keep a CTA's TMEM at 128 columns for n=4, so
+// three CTAs fit an SM's 512 columns.
+constexpr int kAccBufs = 2;
 constexpr int kFlushLag = kAccBufs - 1;
+// CTAs per SM the GEMM is compiled for: three for n=4 (their registers must fit a
+// third of the SM's), one otherwise (n=6 runs two CTAs per SM within that budget).
+template <int N>
+constexpr int gemm_min_ctas() { return N <= 48 ? 3 : 1; }
 
 template <int N>
 struct GemmCfg {
@@ -186,7 +192,7 @@ struct GemmCfg {
 };
 
 template <int DT, int N>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, gemm_min_ctas<N>())
     gemm_sumsq_kernel(const __grid_constant__ CUtensorMap xMap, const __grid_constant__ CUtensorMap phiMap,
                       const GemmParams p) {
     // Persistent: CTA b processes the work items (row tile, K split) b, b+G, b+2G, ...
@@ -240,7 +246,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // the epilogue grid may start launching now; it waits for this grid in-kernel
     grid_launch_dependents();
     const uint32_t tacc = *tmemSlot;
-    const bool prepared = p.hdr->magic == kPreparedMagic;
+    const bool prepared = p.hdr->magic == kPreparedMagic && p.hdr->signature == p.signature;
     if (!prepared && threadIdx.x == 0) set_device_status(MHC_STATUS_NOT_PREPARED);
 
     auto stage_x = [&](int s) { return smem + static_cast<size_t>(s) * Cfg::kStageBytes; };
@@ -670,6 +676,7 @@ static int launch_fused(const Problem& p, const Plan& plan, const CUtensorMap& x
     fp.hpre = reinterpret_cast<float*>(ws + plan.hpreOffset);
     fp.cnt = reinterpret_cast<unsigned*>(ws + plan.cntOffset);
     fp.hdr = reinterpret_cast<const WorkspaceHeader*>(workspace);
+    fp.signature = p.signature;
     if (evBegin != nullptr && cudaEventRecord(evBegin, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
     const bool bf = p.dtype == MHC_DTYPE_BF16;
     int rc;
@@ -728,6 +735,7 @@ static int launch_decode(const Problem& p, const Plan& plan, const void* x, cons
     dp.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.partOffset);
     dp.barrier = &hdr->gridBarrier;
     dp.hdr = hdr;
+    dp.signature = p.signature;
     if (evBegin != nullptr && cudaEventRecord(evBegin, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
     const bool bf = p.dtype == MHC_DTYPE_BF16;
     int rc;
@@ -765,6 +773,7 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
     gp.chunks = plan.chunks;
     gp.splits = plan.splits;
     gp.stages = plan.stages;
+    gp.signature = p.signature;
     gp.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.partOffset);
     gp.hdr = reinterpret_cast<const WorkspaceHeader*>(workspace);
     int rc;

@@ -7,7 +7,11 @@ Tolerances (stated by the operator's contract):
   hIn          within 1 ulp of the x dtype; an element may differ by more only where
                the stream sum cancels, i.e. |got - ref| <= 1 ulp + 1e-5 * sum_s |hPre_s x_s|
                (hPre carries the GEMM's ~1e-6 relative error into hIn); the exact-match
-               rate must exceed 99%.
+               rate must exceed 99%.  Beyond K = 32768 the budget grows with K, because
+               fp32 sums over K (the oracle's sequential one included) lose accuracy in
+               proportion; there, instead of the exact-match rate against the oracle,
+               the GPU must be at least as close to a float64 restatement as the oracle
+               is (test_large_head_dims).
 """
 from __future__ import annotations
 
@@ -36,6 +40,7 @@ def np32(t):
 
 def compare(got, x_bits, phi, alpha, bias, gamma, n, D, dtype, label="", norm_eps=1e-6, hc_eps=1e-6):
     """got = (hIn bits [R,D], hPost [R,n], hRes [R,n,n]) for the rows in x_bits."""
+    budget = HIN_BUDGET * max(1.0, n * D / 32768)
     g_in, g_post, g_res = got
     r_in, r_post, r_res = ref.mhc_pre_ref(x_bits, phi, alpha, bias, gamma, n, D, dtype, norm_eps, hc_eps)
     stats = {}
@@ -54,9 +59,10 @@ def compare(got, x_bits, phi, alpha, bias, gamma, n, D, dtype, label="", norm_ep
         gf = ref.to_float(g_in, dtype).astype(np.float64)
         rf = ref.to_float(r_in, dtype).astype(np.float64)
         ulp = ref.ulp_size(r_in, dtype)
-        ok = np.abs(gf - rf) <= ulp + HIN_BUDGET * mag
+        ok = np.abs(gf - rf) <= ulp + budget * mag
         assert ok[d > 1].all(), f"{label} hIn differs beyond 1 ulp without cancellation"
-    assert stats["hIn_exact"] > 0.99, f"{label} hIn exact-match rate {stats['hIn_exact']}"
+    if n * D <= 32768:  # beyond, both sides are fp32 approximations: see test_large_head_dims
+        assert stats["hIn_exact"] > 0.99, f"{label} hIn exact-match rate {stats['hIn_exact']}"
     return stats
 
 
@@ -173,6 +179,49 @@ def test_boundary_shapes(shape):
     check_config(cfg)
 
 
+@pytest.mark.parametrize("shape", [s for s in BOUNDARY if s[0] * s[1] <= 32],
+                         ids=lambda s: f"B{s[0]}S{s[1]}n{s[2]}D{s[3]}g{int(s[4])}{s[5]}")
+def test_boundary_shapes_split_k_path(shape, monkeypatch):
+    """The smallest shapes run the decode kernel by default; the split-K path must
+    handle them too (one 64-wide chunk or a partial one, one ragged row tile)."""
+    monkeypatch.setenv("MHC_PRE_PATH", "0")
+    B, S, n, D, g, dt = shape
+    cfg = Config("boundary_splitk", B, S, n, D, dt, 0.05, g, seed=12)
+    assert mp.query_plan(mp.make_desc(B, S, n, D, mp.BF16 if dt == "bf16" else mp.F16, g))["path"] == 0
+    check_config(cfg)
+
+
+LARGE_D = [
+    Config("large_d_decode", 1, 3, 4, 32768, "bf16", 0.005, True, seed=21),     # K = 131072 on the decode path
+    Config("large_d_splitk", 1, 200, 8, 16384, "fp16", 0.002, False, seed=22),  # K = 131072, mix 80, split-K
+    Config("large_d_n6", 1, 150, 6, 16400, "bf16", 0.002, True, seed=23),       # D % 64 == 16
+]
+
+
+@pytest.mark.parametrize("cfg", LARGE_D, ids=lambda c: c.name)
+def test_large_head_dims(cfg):
+    check_config(cfg)
+    # accuracy against a float64 restatement: no worse than the oracle's own
+    inp = make_inputs(cfg)
+    hIn, hPost, _ = run_op(inp)
+    M, n, D = cfg.M, cfg.n, cfg.D
+    xb = bits(inp["x"].reshape(M, n * D))
+    gamma = np32(inp["gamma"])
+    g = None if gamma is None else gamma.reshape(-1)
+    h64, post64, _, _ = ref.mhc_pre_numpy(xb, np32(inp["phi"]), np32(inp["alpha"]), np32(inp["bias"]), g, n, D,
+                                          cfg.dtype)
+    o_in, o_post, _ = ref.mhc_pre_ref(xb, np32(inp["phi"]), np32(inp["alpha"]), np32(inp["bias"]), g, n, D,
+                                      cfg.dtype)
+    r64 = ref.from_float(h64.astype(np.float32), cfg.dtype)
+    d_gpu = ref.ulp_distance(bits(hIn.reshape(M, D)), r64)
+    d_oracle = ref.ulp_distance(o_in, r64)
+    assert d_gpu.max() <= max(d_oracle.max(), 1) + 1, (d_gpu.max(), d_oracle.max())
+    assert (d_gpu == 0).mean() >= (d_oracle == 0).mean() - 0.002, ((d_gpu == 0).mean(), (d_oracle == 0).mean())
+    gpu_post = np.abs(hPost.reshape(M, n).cpu().numpy() - post64).max()
+    oracle_post = np.abs(o_post - post64).max()
+    assert gpu_post <= 2 * oracle_post + 1e-6, (gpu_post, oracle_post)
+
+
 def test_relaunch_is_idempotent_and_matches_one_shot():
     """E2 analogue (cloud_runner/probe_e1e2.cpp:312-326): relaunching a prepared
     executor gives bit-identical outputs, equal to the one-shot call."""
@@ -231,6 +280,27 @@ def test_error_paths_on_device():
     with pytest.raises(mp.MhcPreError) as ei:
         mp.mhc_pre(xm, inp["phi"], inp["alpha"], inp["bias"], None)
     assert ei.value.status == -7
+    assert mp.device_status() == 0
+
+
+@pytest.mark.parametrize("seq", [4, 64], ids=["decode_path", "split_k_path"])
+def test_weights_prepared_for_another_shape_are_refused(seq):
+    """A workspace holds weights prepared for one (n, D, dtype, gamma); running a
+    different description on it must not compute silently with them: the kernels
+    compare the prepared signature and report MHC_STATUS_NOT_PREPARED."""
+    cfg_a = Config("sig_a", 1, seq, 4, 256, "bf16", 0.02, True, seed=31)
+    cfg_b = Config("sig_b", 1, seq, 4, 512, "bf16", 0.02, True, seed=32)
+    ia, ib = make_inputs(cfg_a), make_inputs(cfg_b)
+    da = mp.make_desc(1, seq, 4, 256, mp.BF16, True)
+    db = mp.make_desc(1, seq, 4, 512, mp.BF16, True)
+    ws = torch.zeros(max(mp.workspace_size(da), mp.workspace_size(db)), dtype=torch.uint8, device="cuda")
+    ex_a = mp.MhcPre(1, seq, 4, 256, torch.bfloat16, True, workspace=ws)
+    ex_a.prepare(ia["phi"], ia["gamma"])
+    ex_b = mp.MhcPre(1, seq, 4, 512, torch.bfloat16, True, workspace=ws)
+    ex_b(ib["x"], ib["alpha"], ib["bias"])  # never prepared for D=512
+    assert mp.device_status() == -12  # MHC_STATUS_NOT_PREPARED
+    ex_b.prepare(ib["phi"], ib["gamma"])
+    ex_b(ib["x"], ib["alpha"], ib["bias"])
     assert mp.device_status() == 0
 
 
