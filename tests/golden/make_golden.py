@@ -99,7 +99,9 @@ def run_case(audit, case):
 
 
 def main(argv):
-    ref_root = Path(argv[1]) if len(argv) > 1 else Path("/root/reference")
+    if len(argv) < 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <reference checkout>")
+    ref_root = Path(argv[1])
     audit = _load_audit(ref_root)
     # the reference's own known-answer test for its rounding helpers must pass first
     audit._self_test_arith()
