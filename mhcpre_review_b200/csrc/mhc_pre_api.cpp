@@ -83,20 +83,19 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     const size_t smemLimit = 232448;  // sm_100 per-block opt-in maximum
     const size_t fixed = 1024 /*alignment slack*/ + 256 /*barriers*/;
     // GEMM CTAs per SM.  One CTA's MMA issue stream retires a tcgen05.mma about every
-    // 145 cycles whatever N is, and a CTA's ring holds only so many bytes in flight,
-    // so more CTAs per SM stream faster, as far as TMEM (two accumulator buffers of N
-    // columns, rounded to a power of two) and registers allow: three for n=4 (the
-    // kernel is compiled for three), two for n=6, one for n=8.  Three CTAs (3 stages
-    // each) pay off when the items fill at least six rounds of them; with fewer, the
-    // 4-stage rings of two CTAs lose less to the last round.
+    // 145 cycles whatever N is, and a CTA's ring streams about stages x 16 KB per TMA
+    // round trip (~2.5 us), so more CTAs per SM stream faster and split the work into
+    // more, smaller shares (the last round of items costs less), as far as TMEM (two
+    // accumulator buffers of N columns, rounded to a power of two), registers and
+    // shared memory allow: four for n=4 (2 stages each; the kernel is compiled for
+    // four), two for n=6, one for n=8.
     const int accCols = 2 * p.N <= 64 ? 64 : 2 * p.N <= 128 ? 128 : 2 * p.N <= 256 ? 256 : 512;
-    const int maxCtas = std::min(512 / accCols, p.N <= 48 ? 3 : 2);
-    const int64_t items = static_cast<int64_t>(pl.tilesM) * splits;
+    const int maxCtas = std::min(512 / accCols, p.N <= 48 ? 4 : 2);
     int ctasPerSm = maxCtas;
-    if (ctasPerSm == 3 && items < 6 * 3 * static_cast<int64_t>(smCount)) ctasPerSm = 2;
     // Tuning override: MHC_PRE_GEMM_CTAS (CTAs per SM, within the limits above).
     if (const char* ct = std::getenv("MHC_PRE_GEMM_CTAS")) ctasPerSm = std::max(1, std::min(std::atoi(ct), maxCtas));
-    const size_t budget = ctasPerSm == 1 ? smemLimit : ctasPerSm == 2 ? 110 * 1024 : 74 * 1024;
+    const size_t budget = ctasPerSm == 1 ? smemLimit : ctasPerSm == 2 ? 110 * 1024 : ctasPerSm == 3 ? 74 * 1024
+                                                                                                        : 55 * 1024;
     int stages = static_cast<int>((budget - fixed) / stageBytes);
     stages = std::max(2, std::min(stages, 8));
     // Tuning override: MHC_PRE_GEMM_STAGES (ring depth).

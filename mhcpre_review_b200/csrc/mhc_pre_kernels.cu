@@ -169,13 +169,13 @@ constexpr int kGemmThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 square-s
 constexpr int kSegChunks = 4;
 // Accumulator buffers: the square-sum warps add segment s-1 into registers while the
 // MMA fills segment s.  Two buffers keep a CTA's TMEM at 128 columns for n=4, so
-// three CTAs fit an SM's 512 columns.
+// four CTAs fit an SM's 512 columns.
 constexpr int kAccBufs = 2;
 constexpr int kFlushLag = kAccBufs - 1;
-// CTAs per SM the GEMM is compiled for: three for n=4 (their registers must fit a
-// third of the SM's), one otherwise (n=6 runs two CTAs per SM within that budget).
+// CTAs per SM the GEMM is compiled for: four for n=4 (their registers must fit a
+// quarter of the SM's), one otherwise (n=6 runs two CTAs per SM within that budget).
 template <int N>
-constexpr int gemm_min_ctas() { return N <= 48 ? 3 : 1; }
+constexpr int gemm_min_ctas() { return N <= 48 ? 4 : 1; }
 
 template <int N>
 struct GemmCfg {
