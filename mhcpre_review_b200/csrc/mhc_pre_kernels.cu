@@ -472,7 +472,9 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
     __shared__ float sMix[mix];
     __shared__ float sPre[NS];
     __shared__ float sSum;
-    const int64_t r = blockIdx.x;
+    // Rows in reverse: the GEMM's last items read the last tiles, whose x is still
+    // partly in L2 when this grid's first CTAs start.
+    const int64_t r = p.M - 1 - blockIdx.x;
     const int tid = threadIdx.x;
     grid_dependency_wait();
     // sum over splits in split order, staged kEpiSplitBlock splits at a time
