@@ -286,8 +286,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) mhc_pre_decode_kernel(const
         v = __fadd_rn(v, p.normEps);
         return __fdiv_rn(1.0f, __fsqrt_rn(v));
     };
+    // warp-major numbering spreads the units over all CTAs (SMs) before doubling up
     const int warps = G * (kDecodeThreads / 32);
-    for (int u = g * (kDecodeThreads / 32) + warp; u < units; u += warps) {
+    for (int u = warp * G + g; u < units; u += warps) {
         if (u < hinUnits) {
             const int m = u / nd, dr = u - (u / nd) * nd;
             // the x loads do not depend on hPre: issue them with the record loads
