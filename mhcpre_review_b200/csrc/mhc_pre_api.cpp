@@ -64,36 +64,38 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     pl.path = 0;
     pl.tilesM = static_cast<int>((p.M + kRowsPerTile - 1) / kRowsPerTile);
     pl.chunks = static_cast<int>((p.K + kChunk - 1) / kChunk);
-    // K splits.  From kShardRows rows up, the split count depends on K only (groups
-    // of at most kGroupChunks chunks), so a row's arithmetic, and therefore its
-    // result bits, do not depend on M: token shards of that size reproduce the
-    // unsharded run exactly.  Smaller problems split further to fill the SMs, down
-    // to kMinSplitChunks chunks per split: below that the epilogue's reduction over
-    // splits costs more than the GEMM CTAs save.
-    const int groups = (pl.chunks + kGroupChunks - 1) / kGroupChunks;
-    int splits = groups;
-    if (p.M < kShardRows && pl.tilesM < smCount)
-        splits = std::max(groups, std::min(smCount / pl.tilesM, std::max(1, pl.chunks / kMinSplitChunks)));
-    // Tuning override: MHC_PRE_SPLITS (K splits of the split-K path).
-    if (const char* sp = std::getenv("MHC_PRE_SPLITS")) splits = std::max(1, std::atoi(sp));
-    splits = std::min(splits, pl.chunks);
-    pl.splits = splits;
-    pl.gemmGrid = std::min(pl.tilesM * splits, smCount);
-    const size_t stageBytes = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + static_cast<size_t>(p.N) * kChunk * 2;
-    const size_t smemLimit = 232448;  // sm_100 per-block opt-in maximum
-    const size_t fixed = 1024 /*alignment slack*/ + 256 /*barriers*/;
     // GEMM CTAs per SM.  One CTA's MMA issue stream retires a tcgen05.mma about every
     // 145 cycles whatever N is, and a CTA's ring streams about stages x 16 KB per TMA
     // round trip (~2.5 us), so more CTAs per SM stream faster and split the work into
-    // more, smaller shares (the last round of items costs less), as far as TMEM (two
-    // accumulator buffers of N columns, rounded to a power of two), registers and
-    // shared memory allow: four for n=4 (2 stages each; the kernel is compiled for
-    // four), two for n=6, one for n=8.
-    const int accCols = 2 * p.N <= 64 ? 64 : 2 * p.N <= 128 ? 128 : 2 * p.N <= 256 ? 256 : 512;
+    // more, smaller shares (the last round of items costs less), as far as TMEM
+    // (the kernel's accumulator buffers of N columns, rounded to a power of two),
+    // registers and shared memory allow: four for n=4 (2 stages each), two for n=6
+    // (two buffers) and for n=8 (one buffer).
+    const int accBufs = p.N > 128 ? 1 : 2;  // GemmCfg<N>::kAccBufs
+    const int accNeed = accBufs * p.N;
+    const int accCols = accNeed <= 64 ? 64 : accNeed <= 128 ? 128 : accNeed <= 256 ? 256 : 512;
     const int maxCtas = std::min(512 / accCols, p.N <= 48 ? 4 : 2);
     int ctasPerSm = maxCtas;
     // Tuning override: MHC_PRE_GEMM_CTAS (CTAs per SM, within the limits above).
     if (const char* ct = std::getenv("MHC_PRE_GEMM_CTAS")) ctasPerSm = std::max(1, std::min(std::atoi(ct), maxCtas));
+    const int slots = ctasPerSm * smCount;
+    // K splits.  From kShardRows rows up, the split count depends on K only (groups
+    // of at most kGroupChunks chunks), so a row's arithmetic, and therefore its
+    // result bits, do not depend on M: token shards of that size reproduce the
+    // unsharded run exactly.  Smaller problems split further to fill the GEMM's CTA
+    // slots, down to kMinSplitChunks chunks per split: below that the epilogue's
+    // reduction over splits costs more than the GEMM CTAs save.
+    const int groups = (pl.chunks + kGroupChunks - 1) / kGroupChunks;
+    int splits = groups;
+    if (p.M < kShardRows && pl.tilesM < slots)
+        splits = std::max(groups, std::min(slots / pl.tilesM, std::max(1, pl.chunks / kMinSplitChunks)));
+    // Tuning override: MHC_PRE_SPLITS (K splits of the split-K path).
+    if (const char* sp = std::getenv("MHC_PRE_SPLITS")) splits = std::max(1, std::atoi(sp));
+    splits = std::min(splits, pl.chunks);
+    pl.splits = splits;
+    const size_t stageBytes = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + static_cast<size_t>(p.N) * kChunk * 2;
+    const size_t smemLimit = 232448;  // sm_100 per-block opt-in maximum
+    const size_t fixed = 1024 /*alignment slack*/ + 256 /*barriers*/;
     const size_t budget = ctasPerSm == 1 ? smemLimit : ctasPerSm == 2 ? 110 * 1024 : ctasPerSm == 3 ? 74 * 1024
                                                                                                         : 55 * 1024;
     int stages = static_cast<int>((budget - fixed) / stageBytes);

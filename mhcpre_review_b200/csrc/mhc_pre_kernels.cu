@@ -167,21 +167,23 @@ constexpr int kGemmThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 square-s
 // K chunks; finished segments are added into IEEE fp32 registers by the epilogue
 // warps while the MMA fills the other accumulator buffer.
 constexpr int kSegChunks = 4;
-// Accumulator buffers: the square-sum warps add segment s-1 into registers while the
-// MMA fills segment s.  Two buffers keep a CTA's TMEM at 128 columns for n=4, so
-// four CTAs fit an SM's 512 columns.
-constexpr int kAccBufs = 2;
-constexpr int kFlushLag = kAccBufs - 1;
-// CTAs per SM the GEMM is compiled for: four for n=4 (their registers must fit a
-// quarter of the SM's), one otherwise (n=6 runs two CTAs per SM within that budget).
+// CTAs per SM the GEMM is compiled for (their registers must fit that share of the
+// SM's): four for n=4, two for n=8, one for n=6 (which runs two within that budget).
 template <int N>
-constexpr int gemm_min_ctas() { return N <= 48 ? 4 : 1; }
+constexpr int gemm_min_ctas() { return N <= 48 ? 4 : N > 128 ? 2 : 1; }
 
 template <int N>
 struct GemmCfg {
     static constexpr int kXBytes = kRowsPerTile * kChunk * 2;  // 16 KB
     static constexpr int kPhiBytes = N * kChunk * 2;          // N rows x 128 B
     static constexpr int kStageBytes = kXBytes + kPhiBytes;
+    // Accumulator buffers: with two, the square-sum warps add segment s-1 into
+    // registers while the MMA fills segment s; two buffers keep a CTA's TMEM at 128
+    // columns for n=4 (four CTAs per SM) and 256 for n=6 (two).  n=8 (N=160) keeps
+    // one, so that two CTAs fit the SM's 512 columns: the MMA then waits for each
+    // flush, which the other CTA covers.
+    static constexpr int kAccBufs = N > 128 ? 1 : 2;
+    static constexpr int kFlushLag = kAccBufs - 1;
     // kAccBufs accumulator buffers of N fp32 columns each
     static constexpr uint32_t kTmemCols = kAccBufs * N <= 64    ? 64
                                           : kAccBufs * N <= 128 ? 128
@@ -204,6 +206,8 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_min_ctas<N>())
     const int S = p.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * Cfg::kStageBytes);  // [S]
     uint64_t* empty = full + S;
+    constexpr int kAccBufs = Cfg::kAccBufs;
+    constexpr int kFlushLag = Cfg::kFlushLag;
     uint64_t* accFull = empty + S;            // [kAccBufs]
     uint64_t* accEmpty = accFull + kAccBufs;  // [kAccBufs]
     uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(accEmpty + kAccBufs);
