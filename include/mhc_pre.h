@@ -157,7 +157,8 @@ MHC_API int mhcPreRunNoAlloc(const mhcPreDesc_t* desc, const void* x, const floa
  * benchmarks and profiling; no reference counterpart). */
 typedef struct {
     int32_t path;           /* 0 = split-K GEMM + epilogue kernels, 1 = fused team kernel
-                               (opt-in), 2 = single-launch decode kernel (M <= 32) */
+                               (opt-in), 2 = single-launch decode kernel (M <= 32),
+                               3 = cluster-team kernel (opt-in) */
     int32_t kernelsPerRun;  /* kernels launched by mhcPreRunPrepared */
     int32_t gridCtas;       /* CTAs of the main kernel */
     int32_t splits;         /* K splits (paths 0 and 2) or team size (path 1) */

@@ -131,6 +131,48 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
         }
     }
 
+    // Path 3, the cluster-team kernel (opt-in: MHC_PRE_PATH=3), when D splits into
+    // 64-wide chunks evenly over a cluster of S = 16 (or 8) CTAs.  The teams are as
+    // many clusters as fit on the device at once.
+    {
+        const char* fp = std::getenv("MHC_PRE_PATH");
+        if (fp != nullptr && fp[0] == '3' && p.D % kChunk == 0) {
+            const int dc = static_cast<int>(p.D / kChunk);
+            const int S = dc % 16 == 0 ? 16 : dc % 8 == 0 ? 8 : 0;
+            if (S > 0) {
+                Plan c = pl;
+                c.path = 3;
+                c.teamS = S;
+                c.J = dc / S;
+                c.splits = 1;
+                const size_t gStage = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + static_cast<size_t>(p.N) * kChunk * 2;
+                const size_t hStage = static_cast<size_t>(kRowsPerTile) * kChunk * 2;
+                // ring depths: the hIn ring shrinks (4 -> 2) until a GEMM ring of >= 2 fits
+                const size_t fixed = 1024 + cluster_extra(p);
+                c.hStages = 0;
+                for (int hs = 4; hs >= 2; --hs) {
+                    if (fixed + hs * hStage + 2 * gStage > 232448) continue;
+                    c.hStages = hs;
+                    c.gStages = std::min(6, static_cast<int>((232448 - fixed - hs * hStage) / gStage));
+                    break;
+                }
+                c.smemBytes = fixed + c.gStages * gStage + c.hStages * hStage;
+                c.partOffset = align_up(pl.phiOffset + pl.phiBytes, 256);
+                c.partBytes = 0;
+                c.hpreOffset = c.partOffset;
+                c.cntOffset = c.partOffset;
+                c.cntBytes = 256;  // the global abort word
+                c.totalBytes = c.cntOffset + c.cntBytes;
+                int teams = 0;
+                if (c.hStages > 0 && cluster_max_teams(p, c, &teams) == 0 && teams > 0) {
+                    c.teams = std::min(teams, c.tilesM);
+                    *plan = c;
+                    return MHC_STATUS_SUCCESS;
+                }
+            }
+        }
+    }
+
     // Path 1, the fused kernel, when D splits into 64-wide chunks evenly over a team
     // (a row's arithmetic depends on the team size S only, not on M).  S divides
     // D/64.  Its hIn pass re-reads x from L2, which can hit only while the tiles the
@@ -368,10 +410,11 @@ int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* out) {
     std::memset(out, 0, sizeof(*out));
     out->path = plan.path;
     out->kernelsPerRun = plan.path == 0 ? 2 : 1;
-    out->gridCtas = plan.path == 1 ? plan.teams * plan.teamS : plan.gemmGrid;
-    out->splits = plan.path == 1 ? plan.teamS : plan.splits;
+    const bool teamPath = plan.path == 1 || plan.path == 3;
+    out->gridCtas = teamPath ? plan.teams * plan.teamS : plan.gemmGrid;
+    out->splits = teamPath ? plan.teamS : plan.splits;
     out->rowsPerTile = kRowsPerTile;
-    out->reserved[0] = plan.path == 1 ? plan.teams : 0;
+    out->reserved[0] = teamPath ? plan.teams : 0;
     return MHC_STATUS_SUCCESS;
 }
 

@@ -49,7 +49,8 @@ struct Problem {
 };
 
 struct Plan {
-    int path;        // 0: split-K GEMM + epilogue kernels, 1: fused team kernel, 2: decode kernel
+    int path;        // 0: split-K GEMM + epilogue kernels, 1: fused team kernel, 2: decode kernel,
+                     // 3: cluster-team kernel
     int tilesM;      // ceil(M / 128)
     int chunks;      // ceil(K / 64)
     int splits;      // K splits (path 0)
@@ -76,6 +77,8 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
 int read_and_clear_device_status(int32_t* status);
 size_t decode_smem(const Problem& p);  // dynamic shared memory of the decode kernel
 int diag_wait_timeout(uint64_t limit_ns, int* result_host, cudaStream_t stream);
+size_t cluster_extra(const Problem& p);  // cluster kernel's shared memory beyond its rings
+int cluster_max_teams(const Problem& p, const Plan& plan, int* teams);
 
 // Validation + plan for the current device, and prepare-then-run into a given
 // workspace (used by the no-allocation entry point).

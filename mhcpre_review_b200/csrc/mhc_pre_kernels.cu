@@ -558,6 +558,7 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
 }
 
 #include "mhc_pre_fused.cuh"
+#include "mhc_pre_cluster.cuh"
 #include "mhc_pre_decode.cuh"
 
 // ---------------------------------------------------------------------------
@@ -760,6 +761,119 @@ static int launch_decode(const Problem& p, const Plan& plan, const void* x, cons
 
 size_t decode_smem(const Problem& p) { return decode_smem_bytes(static_cast<int>(p.M), p.mix); }
 
+size_t cluster_extra(const Problem& p) { return cluster_extra_smem(p.W); }
+
+template <int DT, int NS>
+static cudaError_t cluster_prepare_attrs(const Plan& plan) {
+    auto kern = mhc_pre_cluster_kernel<DT, NS>;
+    static std::atomic<int> setBytes[kMaxDevices];
+    cudaError_t e = ensure_smem(kern, setBytes, plan.smemBytes);
+    if (e != cudaSuccess) return e;
+    if (plan.teamS > 8) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    return e;
+}
+
+template <int DT, int NS>
+static int cluster_teams_t(const Plan& plan, int* teams) {
+    cudaError_t e = cluster_prepare_attrs<DT, NS>(plan);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.teamS), 1, 1);
+    cfg.blockDim = dim3(kClusterThreads, 1, 1);
+    cfg.dynamicSmemBytes = plan.smemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(plan.teamS);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, mhc_pre_cluster_kernel<DT, NS>, &cfg);
+    if (e != cudaSuccess) return e;
+    *teams = n;
+    return 0;
+}
+
+// Clusters of plan.teamS CTAs that fit on the device at once (the persistent teams).
+int cluster_max_teams(const Problem& p, const Plan& plan, int* teams) {
+    const bool bf = p.dtype == MHC_DTYPE_BF16;
+    switch (p.n) {
+        case 4: return bf ? cluster_teams_t<MHC_DTYPE_BF16, 4>(plan, teams) : cluster_teams_t<MHC_DTYPE_F16, 4>(plan, teams);
+        case 6: return bf ? cluster_teams_t<MHC_DTYPE_BF16, 6>(plan, teams) : cluster_teams_t<MHC_DTYPE_F16, 6>(plan, teams);
+        default: return bf ? cluster_teams_t<MHC_DTYPE_BF16, 8>(plan, teams) : cluster_teams_t<MHC_DTYPE_F16, 8>(plan, teams);
+    }
+}
+
+template <int DT, int NS>
+static int launch_cluster_t(const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
+                            const ClusterParams& cp, cudaStream_t stream) {
+    cudaError_t e = cluster_prepare_attrs<DT, NS>(plan);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.teams * plan.teamS), 1, 1);
+    cfg.blockDim = dim3(kClusterThreads, 1, 1);
+    cfg.dynamicSmemBytes = plan.smemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(plan.teamS);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, mhc_pre_cluster_kernel<DT, NS>, xMap, phiMap, cp);
+}
+
+static int launch_cluster(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
+                          const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes, void* workspace,
+                          cudaStream_t stream, cudaEvent_t evBegin, cudaEvent_t evEnd) {
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaError_t e = cudaMemsetAsync(ws + plan.cntOffset, 0, plan.cntBytes, stream);
+    if (e != cudaSuccess) return e;
+    ClusterParams cp;
+    cp.M = p.M;
+    cp.D = p.D;
+    cp.J = plan.J;
+    cp.S = plan.teamS;
+    cp.T = plan.teams;
+    cp.tilesM = plan.tilesM;
+    cp.W = p.W;
+    cp.gStages = plan.gStages;
+    cp.hStages = plan.hStages;
+    {
+        const char* hm = std::getenv("MHC_PRE_L2HINT");  // tuning override: 0, 1 or 2
+        cp.l2mode = hm != nullptr ? std::atoi(hm) : 1;
+        const char* ld = std::getenv("MHC_PRE_LEAD");    // tuning override: chunks
+        cp.lead = ld != nullptr ? std::max(1, std::atoi(ld)) : plan.gStages + 2;
+    }
+    cp.invK = 1.0f / static_cast<float>(p.K);
+    cp.normEps = p.normEps;
+    cp.hcEps = p.hcEps;
+    cp.alpha = alpha;
+    cp.bias = bias;
+    cp.hIn = static_cast<uint16_t*>(hIn);
+    cp.hPost = hPost;
+    cp.hRes = hRes;
+    cp.gAbort = reinterpret_cast<unsigned*>(ws + plan.cntOffset);
+    cp.hdr = reinterpret_cast<const WorkspaceHeader*>(workspace);
+    cp.signature = p.signature;
+    if (evBegin != nullptr && cudaEventRecord(evBegin, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    const bool bf = p.dtype == MHC_DTYPE_BF16;
+    int rc;
+    switch (p.n) {
+        case 4: rc = bf ? launch_cluster_t<MHC_DTYPE_BF16, 4>(plan, xMap, phiMap, cp, stream)
+                        : launch_cluster_t<MHC_DTYPE_F16, 4>(plan, xMap, phiMap, cp, stream); break;
+        case 6: rc = bf ? launch_cluster_t<MHC_DTYPE_BF16, 6>(plan, xMap, phiMap, cp, stream)
+                        : launch_cluster_t<MHC_DTYPE_F16, 6>(plan, xMap, phiMap, cp, stream); break;
+        default: rc = bf ? launch_cluster_t<MHC_DTYPE_BF16, 8>(plan, xMap, phiMap, cp, stream)
+                         : launch_cluster_t<MHC_DTYPE_F16, 8>(plan, xMap, phiMap, cp, stream); break;
+    }
+    if (rc != 0) return rc;
+    if (evEnd != nullptr && cudaEventRecord(evEnd, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    return 0;
+}
+
 int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
                const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
                void* workspace, cudaStream_t stream, cudaEvent_t evBegin, cudaEvent_t evEnd) {
@@ -767,6 +881,8 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
         return launch_fused(p, plan, xMap, phiMap, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
     if (plan.path == 2)
         return launch_decode(p, plan, x, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
+    if (plan.path == 3)
+        return launch_cluster(p, plan, xMap, phiMap, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
     GemmParams gp;
     gp.M = p.M;
     gp.tilesM = plan.tilesM;
