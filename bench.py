@@ -7,9 +7,11 @@ config 4, M = 65536 tokens (B=16, S=4096), n=4, D=7168, bf16, gamma on) with the
 weights prepared once beforehand (they are model parameters).  With N GPUs the
 batch's tokens are sharded: rank r takes the contiguous rows shard_range(M, N, r)
 (phi replicated, no collective on the data path), so the total work is fixed and
-scaling is strong; value = M / the slowest rank's device time.  Inputs (3.76 GB of
-x on one GPU, 0.47 GB per GPU at N=8) are larger than the 126 MB L2, so no flush
-is needed between steps.
+scaling is strong; value = M / the slowest rank's device time.  Config 4's inputs
+(3.76 GB of x on one GPU, 0.47 GB per GPU at N=8) are larger than the 126 MB L2, so
+no flush is needed between steps.  Smaller shards (x under 2x L2, e.g. --config c2)
+get a 256 MB L2 flush before every step, outside that step's CUDA events, and the
+step time is the sum of the steps' own events.
 
 The JSON line also carries:
   roofline      the main kernel's algorithmic bytes per launch / its average launch
@@ -65,6 +67,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--batch", type=int, default=0, help="override the config's batch (profiling cases)")
     ap.add_argument("--decode-sweep", action="store_true", help="config 5 latency sweep (its own JSON line)")
+    ap.add_argument("--no-flush", action="store_true",
+                    help="time small shards with a warm L2 (no flush between steps; not a headline number)")
     return ap.parse_args()
 
 
@@ -211,14 +215,33 @@ def cpu_sample_rows(cfg, x, phi, alpha, bias, gamma, threads, target_s=10.0):
     return int(max(probe, min(len(x), target_s / per_row)))
 
 
-def workload_config(cfg, n_gpus):
+# Below this many bytes of x per GPU (2x the 126 MB L2) the timed steps are separated
+# by an L2 flush (a 256 MB write, outside the step's CUDA events).
+FLUSH_BELOW_BYTES = 252 << 20
+FLUSH_BYTES = 256 << 20
+
+
+def needs_flush(cfg, rows):
+    return rows * cfg.K * 2 < FLUSH_BELOW_BYTES
+
+
+def workload_config(cfg, n_gpus, flushed=None):
     from mhcpre_review_b200.shard import shard_range
     rows = shard_range(cfg.M, n_gpus, 0)[1]
+    xgb = rows * cfg.K * 2 / 1e9
+    if flushed is None:
+        flushed = needs_flush(cfg, rows)
+    if flushed:
+        l2 = "L2 flushed before every step (a 256 MB write, outside the step's CUDA events; x = %.3f GB per GPU)" % xgb
+    elif needs_flush(cfg, rows):
+        l2 = "warm L2, no flush (--no-flush; x = %.3f GB per GPU fits in L2): not a headline number" % xgb
+    else:
+        l2 = "inputs larger than L2 (x = %.2f GB per GPU), no flush" % xgb
     return {"workload": f"{cfg.name}: M={cfg.M} (B={cfg.batch},S={cfg.seq}) in total, n={cfg.n}, D={cfg.D}, "
                         f"{cfg.dtype}, gamma {'on' if cfg.gamma else 'off'}",
             "tokens_per_gpu": rows, "global_tokens": cfg.M, "streams": cfg.n, "head_dim": cfg.D,
             "parallelism": f"token-sharded x{n_gpus} (contiguous rows), phi replicated, no collective",
-            "l2": "inputs larger than L2 (x = %.2f GB per GPU), no flush" % (rows * cfg.K * 2 / 1e9)}
+            "l2": l2}
 
 
 def run_reference(args, cfg, world, rank):
@@ -422,8 +445,14 @@ def main():
     if pg:
         dist.barrier()
 
+    # Small shards (x under 2x L2): flush L2 between steps and time each step alone.
+    # Every rank decides from the same shard sizes, so all take the same branch.
+    flush = needs_flush(cfg, rows) and not args.no_flush
+    flush_buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda") if flush else None
     ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    op_b = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    op_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     for e in ev_b + ev_e:
         e.record()  # materialise the CUDA events before handing them to the library
     t_start = torch.cuda.Event(enable_timing=True)
@@ -435,12 +464,20 @@ def main():
         torch.cuda.synchronize()
         t_start.record()
         for i in range(args.steps):
+            if flush:
+                flush_buf.fill_(i & 0xFF)
+                op_b[i].record()
             ex.run_profiled(x, inp["alpha"], inp["bias"], out, ev_b[i], ev_e[i])
+            if flush:
+                op_e[i].record()
         t_end.record()
         torch.cuda.synchronize()
         if pg:
             dist.barrier()
     ms_total = t_start.elapsed_time(t_end)
+    if flush:
+        # the steps' own device time, without the flushes between them
+        ms_total = sum(b.elapsed_time(e) for b, e in zip(op_b, op_e))
     main_ms = [b.elapsed_time(e) for b, e in zip(ev_b, ev_e)]
     status = mp.device_status()
     if status != 0:
@@ -497,7 +534,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": cfg.dtype,
             "data": "synthetic (seeded, BASELINE config shapes and distributions)",
-            "config": workload_config(full_cfg, world), "plan": plan,
+            "config": workload_config(full_cfg, world, flushed=flush), "plan": plan,
             "gpu_launches": args.steps * plan["kernels_per_run"],
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
         }
