@@ -496,6 +496,8 @@ def main():
         kernel, kbytes = "mhc_pre_fused", cfg.algorithmic_bytes()
     elif plan["path"] == 2:
         kernel, kbytes = "mhc_pre_decode", cfg.algorithmic_bytes()
+    elif plan["path"] == 4:
+        kernel, kbytes = "mhc_pre_small", cfg.algorithmic_bytes()
     else:
         kernel = "gemm_sumsq"
         kbytes = cfg.M * cfg.K * 2 + 4 * cfg.K * cfg.mix + (4 * cfg.K if cfg.gamma else 0)

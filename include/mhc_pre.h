@@ -157,11 +157,12 @@ MHC_API int mhcPreRunNoAlloc(const mhcPreDesc_t* desc, const void* x, const floa
  * benchmarks and profiling; no reference counterpart). */
 typedef struct {
     int32_t path;           /* 0 = split-K GEMM + epilogue kernels, 1 = fused team kernel
-                               (opt-in), 2 = single-launch decode kernel (M <= 32),
-                               3 = cluster-team kernel (opt-in) */
+                               (opt-in), 2 = single-launch decode kernel (M <= 16),
+                               3 = cluster-team kernel (opt-in), 4 = single-launch
+                               small-batch kernel (16 < M <= 384) */
     int32_t kernelsPerRun;  /* kernels launched by mhcPreRunPrepared */
     int32_t gridCtas;       /* CTAs of the main kernel */
-    int32_t splits;         /* K splits (paths 0 and 2) or team size (path 1) */
+    int32_t splits;         /* K splits (paths 0, 2 and 4) or team size (paths 1 and 3) */
     int32_t rowsPerTile;    /* token rows per tensor-core tile */
     int32_t reserved[3];
 } mhcPrePlan_t;
@@ -170,7 +171,10 @@ MHC_API int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* plan);
 
 /* Reads and clears the device-side error word of the current device (set when
  * a kernel gave up a bounded wait).  Synchronizes the current device.
- * *deviceStatus receives 0 or a negative mhcStatus_t. */
+ * *deviceStatus receives 0 or a negative mhcStatus_t.  After
+ * MHC_STATUS_DEVICE_TIMEOUT the outputs of the calls since the last read are
+ * invalid, and the workspace's weights must be prepared again
+ * (mhcPrePrepareWeights) before the next call on it. */
 MHC_API int mhcPreGetDeviceStatus(int32_t* deviceStatus);
 
 /* Diagnostics for failure detection: launches one kernel that waits, with a limit

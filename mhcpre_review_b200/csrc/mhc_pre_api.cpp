@@ -111,18 +111,53 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     pl.partBytes = static_cast<size_t>(splits) * static_cast<size_t>(p.M) * static_cast<size_t>(p.W) * 4;
     pl.totalBytes = align_up(pl.partOffset + pl.partBytes, 256);
 
-    // Path 2, the decode kernel, for M up to kDecodeMaxRows: one cooperative launch
-    // of one CTA per SM (at most one per 64-wide chunk), CUDA-core partial sums per
-    // K-slice, a grid barrier, then the per-row reduction, epilogue and hIn.
-    // MHC_PRE_PATH=0 or =1 in the environment turns it off (tests, tuning).
+    // Path 2, the decode kernel, by default for M up to kDecodeDefaultRows: one
+    // cooperative launch of one CTA per SM (at most one per 64-wide chunk), CUDA-core
+    // partial sums per K-slice, a grid barrier, then the per-row reduction, epilogue
+    // and hIn.  MHC_PRE_PATH=2 selects it up to kDecodeMaxRows (tests); any other
+    // MHC_PRE_PATH value turns it off.
     {
         const char* fp = std::getenv("MHC_PRE_PATH");
-        if (p.M <= kDecodeMaxRows && (fp == nullptr || fp[0] == '2')) {
+        if ((fp == nullptr && p.M <= kDecodeDefaultRows) || (fp != nullptr && fp[0] == '2' && p.M <= kDecodeMaxRows)) {
             pl.path = 2;
             pl.splits = std::min(smCount, pl.chunks);
             pl.gemmGrid = pl.splits;
             pl.stages = 0;
             pl.smemBytes = decode_smem(p);
+            pl.partOffset = align_up(pl.phiOffset + pl.phiBytes, 256);
+            pl.partBytes = static_cast<size_t>(pl.splits) * static_cast<size_t>(p.M) * static_cast<size_t>(p.W) * 4;
+            pl.totalBytes = align_up(pl.partOffset + pl.partBytes, 256);
+            *plan = pl;
+            return MHC_STATUS_SUCCESS;
+        }
+    }
+
+    // Path 4, the small-batch kernel, by default for kDecodeDefaultRows < M <=
+    // kSmallDefaultRows: one
+    // cooperative launch of one CTA per SM (at most one per 64-wide chunk).  Each CTA
+    // runs the tcgen05 contraction of all T = ceil(M/128) row tiles over its K-slice
+    // (every tile's MMA reads the same weight chunk); after one grid barrier each CTA
+    // reduces the records of its rows (m % G == CTA) and streams their hIn.  It needs
+    // T accumulators of N columns in TMEM.  MHC_PRE_PATH=4 selects it for any M up to
+    // kSmallMaxRows (tests); any other MHC_PRE_PATH value turns it off.  Above
+    // kSmallDefaultRows rows the split-K path is faster: its epilogue spreads the hIn
+    // stream over one CTA per row, while here each SM streams several rows.
+    {
+        const char* fp = std::getenv("MHC_PRE_PATH");
+        const bool forced = fp != nullptr && fp[0] == '4';
+        const int tiles = pl.tilesM;
+        if (((fp == nullptr && p.M > kDecodeDefaultRows && p.M <= kSmallDefaultRows) ||
+             (forced && p.M <= kSmallMaxRows)) &&
+            tiles * p.N <= 512) {
+            pl.path = 4;
+            pl.splits = std::min(smCount, pl.chunks);
+            pl.gemmGrid = pl.splits;
+            const size_t stage = small_stage_bytes(tiles, p.N);
+            const int maxChunks = (pl.chunks + pl.splits - 1) / pl.splits;  // per CTA
+            int stages = static_cast<int>((232448 - small_smem_bytes(tiles, p.N, 0)) / stage);
+            stages = std::max(1, std::min(std::min(stages, 8), maxChunks));
+            pl.stages = stages;
+            pl.smemBytes = small_smem_bytes(tiles, p.N, stages);
             pl.partOffset = align_up(pl.phiOffset + pl.phiBytes, 256);
             pl.partBytes = static_cast<size_t>(pl.splits) * static_cast<size_t>(p.M) * static_cast<size_t>(p.W) * 4;
             pl.totalBytes = align_up(pl.partOffset + pl.partBytes, 256);

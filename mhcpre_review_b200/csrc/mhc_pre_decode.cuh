@@ -1,8 +1,9 @@
 // Path 2: the single-launch decode kernel for small M (included by mhc_pre_kernels.cu
 // inside namespace mhc, after the path-0 kernels whose helpers it uses).
 //
-// At M <= kDecodeMaxRows rows the x . phi' product is about 0.7 M multiply-adds per
-// row: CUDA cores finish it in well under a microsecond, and what costs time is
+// At M <= kDecodeMaxRows rows (the plan's default takes it up to kDecodeDefaultRows)
+// the x . phi' product is about 0.7 M multiply-adds per row: CUDA cores finish it in
+// well under a microsecond, and what costs time is
 // reading phi' once (2.75 MB at n=4, D=7168) and the launches.  So one cooperative
 // launch of G CTAs (one per SM) does everything:
 //   phase 1  CTA g takes the K-slice [g*C/G, (g+1)*C/G) of the C 64-wide chunks,
@@ -100,7 +101,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) mhc_pre_decode_kernel(const
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const int M = p.M;
+    // Without weights prepared for this description the launch returns before the
+    // grid barrier (every CTA reads the same header), so the arrival counter only
+    // ever sees launches of the description it was zeroed for, all with the same G.
     const bool prepared = p.hdr->magic == kPreparedMagic && p.hdr->signature == p.signature;
+    if (!prepared) {
+        if (g == 0 && tid == 0) set_device_status(MHC_STATUS_NOT_PREPARED);
+        return;
+    }
 
     // ---------------- phase 1: partial records of this CTA's K-slice ----------------
     const int c0 = static_cast<int>(static_cast<int64_t>(g) * p.chunks / G);
@@ -246,10 +254,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) mhc_pre_decode_kernel(const
         if (!ok) set_device_status(MHC_STATUS_DEVICE_TIMEOUT);
     }
     __syncthreads();
-    if (*sFlag != 0 || !prepared) {
-        if (!prepared && g == 0 && tid == 0) set_device_status(MHC_STATUS_NOT_PREPARED);
-        return;
-    }
+    if (*sFlag != 0) return;
 
     // ---------------- phase 2: warp units ----------------
     const int nd = static_cast<int>((p.D + kDecodeDRange - 1) / kDecodeDRange);

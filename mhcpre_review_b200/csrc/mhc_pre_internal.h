@@ -17,9 +17,12 @@ struct WorkspaceHeader {
     int32_t phiScaleExp;  // fp16: prepared phi' = phi * 2^exp (bf16: 0)
     uint32_t signature;   // hash of the description the weights were prepared for
     uint32_t maxAbsBits;  // max |phi'| (float bits) during preparation
-    // Arrivals at the decode kernel's grid barrier, summed over all its launches on
-    // this workspace (zeroed with the header when weights are prepared); every
-    // launch adds exactly its grid size.
+    // Arrivals at the grid barrier of the decode and small-batch kernels, summed
+    // over all their launches on this workspace (zeroed with the header when weights
+    // are prepared).  Each launch of either kernel adds its grid size G, and a launch
+    // without prepared weights returns before arriving, so the count stays a
+    // multiple of G.  A launch that gave up the barrier (MHC_STATUS_DEVICE_TIMEOUT)
+    // can leave it off: prepare the weights again before the next launch.
     unsigned long long gridBarrier;
     uint32_t pad[58];
 };
@@ -30,7 +33,24 @@ constexpr int kRowsPerTile = 128;  // token rows per tensor-core tile (MMA M)
 constexpr int kChunk = 64;         // K elements per TMA box / pipeline stage (128 bytes)
 constexpr int kMaxMix = 80;
 constexpr int kFusedSlots = 2;     // record/hPre slots per team in the fused kernel
-constexpr int kDecodeMaxRows = 32; // M up to this runs the single-launch decode kernel
+// Row ranges of the single-launch kernels.  The decode kernel (path 2) handles up to
+// kDecodeMaxRows rows and the small-batch kernel (path 4) up to kSmallMaxRows; by
+// default the plan takes the decode kernel up to kDecodeDefaultRows, the small-batch
+// kernel up to kSmallDefaultRows and the split-K path beyond, where each was the
+// fastest in a CUDA-graph latency sweep on B200 (n=4, D=7168).
+constexpr int kDecodeMaxRows = 32;
+constexpr int kDecodeDefaultRows = 16;
+constexpr int kSmallMaxRows = 512;
+constexpr int kSmallDefaultRows = 384;
+
+// Shared memory of the small-batch kernel (path 4): a ring of stages, each holding
+// the row tiles of one K chunk and that chunk of the prepared weights.
+constexpr size_t small_stage_bytes(int tiles, int N) {
+    return static_cast<size_t>(tiles) * kRowsPerTile * kChunk * 2 + static_cast<size_t>(N) * kChunk * 2;
+}
+constexpr size_t small_smem_bytes(int tiles, int N, int stages) {
+    return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * small_stage_bytes(tiles, N) + 256 /*barriers*/;
+}
 
 // Everything a launch needs, derived once from the description.
 struct Problem {
@@ -50,7 +70,7 @@ struct Problem {
 
 struct Plan {
     int path;        // 0: split-K GEMM + epilogue kernels, 1: fused team kernel, 2: decode kernel,
-                     // 3: cluster-team kernel
+                     // 3: cluster-team kernel, 4: small-batch kernel
     int tilesM;      // ceil(M / 128)
     int chunks;      // ceil(K / 64)
     int splits;      // K splits (path 0)

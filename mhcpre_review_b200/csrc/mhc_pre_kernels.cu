@@ -560,6 +560,7 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
 #include "mhc_pre_fused.cuh"
 #include "mhc_pre_cluster.cuh"
 #include "mhc_pre_decode.cuh"
+#include "mhc_pre_small.cuh"
 
 // ---------------------------------------------------------------------------
 // Launchers
@@ -761,6 +762,68 @@ static int launch_decode(const Problem& p, const Plan& plan, const void* x, cons
 
 size_t decode_smem(const Problem& p) { return decode_smem_bytes(static_cast<int>(p.M), p.mix); }
 
+template <int DT, int NS>
+static int launch_small_t(const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap, const SmallParams& sp,
+                          cudaStream_t stream) {
+    auto kern = mhc_pre_small_kernel<DT, NS>;
+    static std::atomic<int> setBytes[kMaxDevices];
+    cudaError_t e = ensure_smem(kern, setBytes, plan.smemBytes);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.gemmGrid), 1, 1);
+    cfg.blockDim = dim3(kSmallThreads, 1, 1);
+    cfg.dynamicSmemBytes = plan.smemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // the grid barriers need every CTA resident
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, xMap, phiMap, sp);
+}
+
+static int launch_small(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
+                        const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
+                        void* workspace, cudaStream_t stream, cudaEvent_t evBegin, cudaEvent_t evEnd) {
+    auto* hdr = reinterpret_cast<WorkspaceHeader*>(workspace);
+    SmallParams sp;
+    sp.M = static_cast<int>(p.M);
+    sp.tiles = plan.tilesM;
+    sp.chunks = plan.chunks;
+    sp.stages = plan.stages;
+    sp.segChunks = kSegChunks;
+    sp.W = p.W;
+    sp.K = p.K;
+    sp.D = p.D;
+    sp.invK = 1.0f / static_cast<float>(p.K);
+    sp.normEps = p.normEps;
+    sp.hcEps = p.hcEps;
+    sp.signature = p.signature;
+    sp.x = static_cast<const uint16_t*>(x);
+    sp.alpha = alpha;
+    sp.bias = bias;
+    sp.hIn = static_cast<uint16_t*>(hIn);
+    sp.hPost = hPost;
+    sp.hRes = hRes;
+    sp.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.partOffset);
+    sp.barrier = &hdr->gridBarrier;
+    sp.hdr = hdr;
+    if (evBegin != nullptr && cudaEventRecord(evBegin, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    const bool bf = p.dtype == MHC_DTYPE_BF16;
+    int rc;
+    switch (p.n) {
+        case 4: rc = bf ? launch_small_t<MHC_DTYPE_BF16, 4>(plan, xMap, phiMap, sp, stream)
+                        : launch_small_t<MHC_DTYPE_F16, 4>(plan, xMap, phiMap, sp, stream); break;
+        case 6: rc = bf ? launch_small_t<MHC_DTYPE_BF16, 6>(plan, xMap, phiMap, sp, stream)
+                        : launch_small_t<MHC_DTYPE_F16, 6>(plan, xMap, phiMap, sp, stream); break;
+        default: rc = bf ? launch_small_t<MHC_DTYPE_BF16, 8>(plan, xMap, phiMap, sp, stream)
+                         : launch_small_t<MHC_DTYPE_F16, 8>(plan, xMap, phiMap, sp, stream); break;
+    }
+    if (rc != 0) return rc;
+    if (evEnd != nullptr && cudaEventRecord(evEnd, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    return 0;
+}
+
 size_t cluster_extra(const Problem& p) { return cluster_extra_smem(p.W); }
 
 template <int DT, int NS>
@@ -883,6 +946,8 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
         return launch_decode(p, plan, x, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
     if (plan.path == 3)
         return launch_cluster(p, plan, xMap, phiMap, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
+    if (plan.path == 4)
+        return launch_small(p, plan, xMap, phiMap, x, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
     GemmParams gp;
     gp.M = p.M;
     gp.tilesM = plan.tilesM;

@@ -157,7 +157,8 @@ static void run_case(int64_t S, int64_t n, int64_t D, int32_t dtype, int32_t gam
 int main(int argc, char** argv) {
     no_gpu_checks();
     if (!(argc > 1 && strcmp(argv[1], "--no-gpu") == 0)) {
-        run_case(300, 4, 256, MHC_DTYPE_BF16, 1);  /* split-K path, ragged last tile */
+        run_case(700, 4, 256, MHC_DTYPE_BF16, 1);  /* split-K path, ragged last tile */
+        run_case(300, 4, 256, MHC_DTYPE_BF16, 1);  /* small-batch path, ragged last tile */
         run_case(5, 8, 512, MHC_DTYPE_F16, 0);     /* decode path */
     }
     printf("%s (%d failures)\n", failures ? "FAILED" : "OK", failures);

@@ -1,9 +1,9 @@
 """The C ABI from a plain C99 program (tests/c_abi/consumer.c), compiled with gcc
 against include/mhc_pre.h and linked with the library the way a host program that
 called the reference's aclnn pair would link it.  Without a GPU it checks the ABI
-version, status strings and shape rejects; on a B200 it also runs a split-K and a
-decode shape through mhcPreRun / mhcPreRunPrepared and compares them with the C
-oracle on the same inputs."""
+version, status strings and shape rejects; on a B200 it also runs a split-K, a
+small-batch and a decode shape through mhcPreRun / mhcPreRunPrepared and compares
+them with the C oracle on the same inputs."""
 from __future__ import annotations
 
 import shutil
@@ -46,4 +46,4 @@ def test_c_consumer_on_gpu(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr
-    assert "path 0" in r.stdout and "path 2" in r.stdout
+    assert "path 0" in r.stdout and "path 2" in r.stdout and "path 4" in r.stdout

@@ -19,18 +19,21 @@ def _desc(cfg):
     return mp.make_desc(cfg.batch, cfg.seq, cfg.n, cfg.D, mp.BF16 if cfg.dtype == "bf16" else mp.F16, cfg.gamma)
 
 
-@pytest.mark.parametrize("m", [1, 8, 32])
+@pytest.mark.parametrize("m", [1, 8, 16])
 def test_decode_plan(m):
-    cfg = CONFIGS[f"c5_m{m}_g"]
+    cfg = with_shape(CONFIGS["c5_m8_g"], seq=m)
     plan = mp.query_plan(_desc(cfg))
     assert plan["path"] == 2 and plan["kernels_per_run"] == 1
     assert plan["grid_ctas"] == plan["splits"] == min(torch.cuda.get_device_properties(0).multi_processor_count,
                                                        (cfg.n * cfg.D + 63) // 64)
 
 
-def test_decode_plan_boundary():
-    cfg = with_shape(CONFIGS["c5_m32_g"], seq=33)
-    assert mp.query_plan(_desc(cfg))["path"] == 0
+def test_decode_plan_boundary(monkeypatch):
+    base = CONFIGS["c5_m32_g"]
+    assert mp.query_plan(_desc(with_shape(base, seq=17)))["path"] == 4  # the small-batch kernel by default
+    monkeypatch.setenv("MHC_PRE_PATH", "2")  # the decode kernel on request, up to 32 rows
+    assert mp.query_plan(_desc(base))["path"] == 2
+    assert mp.query_plan(_desc(with_shape(base, seq=33)))["path"] == 0
 
 
 CASES = [
@@ -46,7 +49,8 @@ CASES = [
 
 
 @pytest.mark.parametrize("cfg", CASES, ids=lambda c: c.name)
-def test_decode_parity(cfg):
+def test_decode_parity(cfg, monkeypatch):
+    monkeypatch.setenv("MHC_PRE_PATH", "2")  # also above the default range (M <= 16)
     assert mp.query_plan(_desc(cfg))["path"] == 2
     check_config(cfg)
 
@@ -68,7 +72,8 @@ def test_decode_matches_split_k_path(monkeypatch):
     assert float(same) > 0.99
 
 
-def test_decode_deterministic_and_repeated_launches():
+def test_decode_deterministic_and_repeated_launches(monkeypatch):
+    monkeypatch.setenv("MHC_PRE_PATH", "2")
     cfg = CONFIGS["c5_m32_ng"]
     inp = make_inputs(cfg)
     x = inp["x"]

@@ -182,8 +182,8 @@ def test_boundary_shapes(shape):
 @pytest.mark.parametrize("shape", [s for s in BOUNDARY if s[0] * s[1] <= 32],
                          ids=lambda s: f"B{s[0]}S{s[1]}n{s[2]}D{s[3]}g{int(s[4])}{s[5]}")
 def test_boundary_shapes_split_k_path(shape, monkeypatch):
-    """The smallest shapes run the decode kernel by default; the split-K path must
-    handle them too (one 64-wide chunk or a partial one, one ragged row tile)."""
+    """The smallest shapes run a single-launch kernel by default; the split-K path
+    must handle them too (one 64-wide chunk or a partial one, one ragged row tile)."""
     monkeypatch.setenv("MHC_PRE_PATH", "0")
     B, S, n, D, g, dt = shape
     cfg = Config("boundary_splitk", B, S, n, D, dt, 0.05, g, seed=12)
@@ -283,7 +283,7 @@ def test_error_paths_on_device():
     assert mp.device_status() == 0
 
 
-@pytest.mark.parametrize("seq", [4, 64], ids=["decode_path", "split_k_path"])
+@pytest.mark.parametrize("seq", [4, 64, 1024], ids=["decode_path", "small_batch_path", "split_k_path"])
 def test_weights_prepared_for_another_shape_are_refused(seq):
     """A workspace holds weights prepared for one (n, D, dtype, gamma); running a
     different description on it must not compute silently with them: the kernels
