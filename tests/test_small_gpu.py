@@ -60,6 +60,8 @@ CASES = [
     Config("sm_n6_m40_k_ragged", 1, 40, 6, 1040, "bf16", 0.01, True, seed=27),       # K % 64 == 32
     Config("sm_n4_m96_few_chunks", 1, 96, 4, 256, "bf16", 0.02, False, seed=28),     # 16 chunks < SMs
     Config("sm_n4_m100_long_k", 1, 100, 4, 32768, "bf16", 0.005, True, seed=29),     # 14 chunks per CTA: 4 segments
+    Config("sm_n4_m40_one_chunk", 1, 40, 4, 16, "fp16", 0.05, True, seed=30),        # K=64: G=1, empty quarters
+    Config("sm_n8_m130_two_chunks", 1, 130, 8, 16, "bf16", 0.05, False, seed=31),    # K=128: G=2, 2 tiles
 ]
 
 
