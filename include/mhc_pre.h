@@ -128,7 +128,7 @@ MHC_API int mhcPreRunPreparedProfiled(const mhcPreDesc_t* desc, const void* x, c
                                       void* stream, void* mainKernelBegin, void* mainKernelEnd);
 
 /* Size of the library's fixed device scratch area used by mhcPreRunNoAlloc. */
-#define MHC_PRE_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+#define MHC_PRE_NOALLOC_SCRATCH_BYTES (96u * 1024u * 1024u)
 
 /* mhcPreRun for callers that cannot allocate device memory while they run: a
  * plugin handed only its tensors' device pointers and no allocator, a serving
@@ -136,11 +136,11 @@ MHC_API int mhcPreRunPreparedProfiled(const mhcPreDesc_t* desc, const void* x, c
  * latency-critical loop that must not call cudaMalloc (it can synchronize the
  * device).  Same inputs, outputs and results as mhcPreRun, but no workspace
  * argument: the prepared weights and the split-K partial records live in one
- * 64 MiB array (MHC_PRE_NOALLOC_SCRATCH_BYTES) compiled into the library, which
+ * 96 MiB array (MHC_PRE_NOALLOC_SCRATCH_BYTES) compiled into the library, which
  * every GPU that loads the library keeps until the process exits.  A problem
  * whose mhcPreGetWorkspaceSize exceeds that size is rejected with
  * MHC_STATUS_TOO_LARGE before anything runs (config 4, M = 65536, n = 4,
- * D = 7168, needs 54 MB and fits).  The call itself allocates nothing: no
+ * D = 7168, needs 65.6 MiB and fits).  The call itself allocates nothing: no
  * cudaMalloc, no cudaFree, no allocating library routine.  The first call on a
  * device looks up that device's copy of the array (cudaGetSymbolAddress, which
  * may load the library's device code); make that first call before any stream

@@ -4,7 +4,7 @@ Some callers cannot hand the operator a workspace: a plugin that receives only i
 tensors' device pointers and no allocator, a serving runtime whose device memory is
 planned and locked before traffic starts, or a latency-critical loop that must not
 call cudaMalloc because it can synchronize the device.  For them the library keeps
-the workspace in one fixed 64 MiB device array of its own and the call allocates
+the workspace in one fixed 96 MiB device array of its own and the call allocates
 nothing.
 
 This file is named so pytest collects it last.  It checks, through the C ABI, that
@@ -109,11 +109,17 @@ def test_no_alloc_entry_matches_workspace_entry_twice():
     assert mp.device_status() == 0
 
 
+SCRATCH_BYTES = 96 * 1024 * 1024  # MHC_PRE_NOALLOC_SCRATCH_BYTES in include/mhc_pre.h
+
+
 def test_no_alloc_rejects_problems_larger_than_the_scratch_array():
-    # D = 7184 is not a multiple of 64, so this runs on the split-K path, whose
-    # partial records grow with M: about 117 MB of workspace at M = 131072
+    # config 4 itself fits, as the header promises
+    c4 = CONFIGS["c4"]
+    assert mp.workspace_size(mp.make_desc(c4.batch, c4.seq, c4.n, c4.D, mp.BF16, True)) <= SCRATCH_BYTES
+    # twice its rows do not: the split-K path's partial records grow with M (about
+    # 126 MiB of workspace at M = 131072)
     cfg = with_shape(CONFIGS["c4"], batch=32, D=7184)
     d = mp.make_desc(cfg.batch, cfg.seq, cfg.n, cfg.D, mp.BF16, True)
-    assert mp.workspace_size(d) > 64 * 1024 * 1024
+    assert mp.workspace_size(d) > SCRATCH_BYTES
     rc = mp.lib().mhcPreRunNoAlloc(ctypes.byref(d), None, None, None, None, None, None, None, None, _stream())
     assert rc == -13  # MHC_STATUS_TOO_LARGE, before any pointer is touched
