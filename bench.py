@@ -67,6 +67,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--batch", type=int, default=0, help="override the config's batch (profiling cases)")
     ap.add_argument("--decode-sweep", action="store_true", help="config 5 latency sweep (its own JSON line)")
+    ap.add_argument("--post", action="store_true",
+                    help="the mHC post step (mhcPostRun) at the config's shape (its own JSON line, one GPU)")
     ap.add_argument("--no-flush", action="store_true",
                     help="time small shards with a warm L2 (no flush between steps; not a headline number)")
     return ap.parse_args()
@@ -338,6 +340,56 @@ def measure_e2e(mp, inp, cfg, steps, pg, dist, world, total_tokens):
             "ms_per_step": ms, "chunks": chunks, "pinned_host": True}
 
 
+def post_step(args):
+    """The mHC post step after the layer (mhcPostRun) at the config's shape on one GPU:
+    xNext = hRes-mix of x + hPost * y.  Inputs (x, y: 4.7 GB at config 4) are larger
+    than L2, so no flush; CUDA events around the K timed calls."""
+    import torch
+    import mhcpre_review_b200 as mp
+    from mhcpre_review_b200.configs import CONFIGS, with_shape
+    torch.cuda.set_device(0)
+    cfg = CONFIGS[args.config]
+    if args.batch > 0:
+        cfg = with_shape(cfg, batch=args.batch, name=f"{cfg.name}_b{args.batch}")
+    dt = torch.bfloat16 if cfg.dtype == "bf16" else torch.float16
+    g = torch.Generator(device="cuda")
+    g.manual_seed(cfg.seed * 1000003 + 11)
+    x = torch.randn((cfg.batch, cfg.seq, cfg.n, cfg.D), generator=g, device="cuda", dtype=dt)
+    y = torch.randn((cfg.batch, cfg.seq, cfg.D), generator=g, device="cuda", dtype=dt)
+    hPost = 2.0 * torch.sigmoid(torch.randn((cfg.batch, cfg.seq, cfg.n), generator=g, device="cuda"))
+    hRes = 0.5 * torch.randn((cfg.batch, cfg.seq, cfg.n, cfg.n), generator=g, device="cuda")
+    out = torch.empty_like(x)
+    for _ in range(max(args.warmup, 3)):
+        mp.mhc_post(x, y, hPost, hRes, out=out)
+    torch.cuda.synchronize()
+    b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        torch.cuda.synchronize()
+        b.record()
+        for _ in range(args.steps):
+            mp.mhc_post(x, y, hPost, hRes, out=out)
+        e.record()
+        torch.cuda.synchronize()
+    if mp.device_status() != 0:
+        raise RuntimeError("device status")
+    ms = b.elapsed_time(e) / args.steps
+    M, n, D = cfg.M, cfg.n, cfg.D
+    nbytes = M * n * D * 2 * 2 + M * D * 2 + 4 * M * (n + n * n)
+    peak, kind = measured_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "mHC post step (mhcPostRun) tokens/s and HBM GB/s", "value": M / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": cfg.dtype, "data": "synthetic (seeded)",
+        "config": {"workload": f"{cfg.name} shape: M={M}, n={n}, D={D}, {cfg.dtype}",
+                   "l2": "inputs larger than L2 (x + y = %.2f GB), no flush" % ((M * n * D + M * D) * 2 / 1e9)},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "kernel": "mhc_post", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "algorithmic_bytes_per_launch": nbytes},
+        "clocks": clocks.summary()}), flush=True)
+
+
 def decode_sweep(args):
     """p50 latency per M, flushed and unflushed L2."""
     import torch
@@ -397,6 +449,9 @@ def main():
     args = parse()
     if args.decode_sweep:
         decode_sweep(args)
+        return
+    if args.post:
+        post_step(args)
         return
     world, rank, local = dist_env()
     from mhcpre_review_b200.configs import CONFIGS, with_shape as _ws

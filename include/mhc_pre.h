@@ -187,6 +187,22 @@ MHC_API int mhcPreGetDeviceStatus(int32_t* deviceStatus);
 MHC_API int mhcPreDiagWaitTimeout(uint32_t limitMicroseconds, int32_t* countersGaveUp, int32_t* barriersGaveUp,
                                   void* stream);
 
+/* The mHC post step that follows MhcPre in a layer: once the layer has turned
+ * hIn into its output y, the residual streams advance as
+ *     xNext[m][s][:] = sum_t hRes[m][s][t] * x[m][t][:] + hPost[m][s] * y[m][:]
+ * with x [B,S,n,D] and y [B,S,D] in the description's 16-bit dtype, hPost [B,S,n]
+ * and hRes [B,S,n,n] fp32 (as mhcPreRun writes them) and xNext [B,S,n,D] in the x
+ * dtype.  Arithmetic: fp32, the first stream's term a rounded product, each
+ * further term (streams in order, then y) one fused multiply-add, one
+ * round-to-nearest-even at the end.  xNext may be x itself (in place); y must not
+ * overlap xNext.  The description's gamma flag and eps values are ignored.  Needs
+ * no workspace and allocates nothing; asynchronous on the stream.  The reference
+ * has no code for this step (it stops at hIn/hPost/hRes), so there is no
+ * counterpart to cite and its results are checked against this library's own C
+ * restatement. */
+MHC_API int mhcPostRun(const mhcPreDesc_t* desc, const void* x, const void* y, const float* hPost,
+                       const float* hRes, void* xNext, void* stream);
+
 /* Human-readable name of a status code (static string). */
 MHC_API const char* mhcPreStatusString(int status);
 

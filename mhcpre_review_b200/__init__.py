@@ -34,7 +34,7 @@ STATUS_NAMES = {
 EXPORTED_SYMBOLS = (
     "mhcPreGetWorkspaceSize", "mhcPrePrepareWeights", "mhcPreRun", "mhcPreRunPrepared",
     "mhcPreRunPreparedProfiled", "mhcPreQueryPlan", "mhcPreGetDeviceStatus", "mhcPreStatusString",
-    "mhcPreAbiVersion", "mhcPreRunNoAlloc", "mhcPreDiagWaitTimeout",
+    "mhcPreAbiVersion", "mhcPreRunNoAlloc", "mhcPreDiagWaitTimeout", "mhcPostRun",
 )
 
 
@@ -81,6 +81,7 @@ def lib():
         L.mhcPreRunPreparedProfiled.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp, sz, vp, vp, vp]
         L.mhcPreQueryPlan.argtypes = [dp, ctypes.POINTER(MhcPrePlan)]
         L.mhcPreRunNoAlloc.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
+        L.mhcPostRun.argtypes = [dp, vp, vp, vp, vp, vp, vp]
         L.mhcPreGetDeviceStatus.argtypes = [ctypes.POINTER(ctypes.c_int32)]
         L.mhcPreStatusString.argtypes = [ctypes.c_int]
         L.mhcPreStatusString.restype = ctypes.c_char_p
@@ -221,3 +222,30 @@ def mhc_pre(x, phi, alpha, bias, gamma=None, norm_eps=1e-6, hc_eps=1e-6, out=Non
                            _ptr(hIn), _ptr(hPost), _ptr(hRes), _ptr(ex.workspace), ex.ws_bytes,
                            _stream_ptr(stream)), "Run")
     return hIn, hPost, hRes
+
+
+def mhc_post(x, y, hPost, hRes, out=None, stream=None):
+    """The mHC post step after the layer: xNext[..., s, :] = sum_t hRes[..., s, t] *
+    x[..., t, :] + hPost[..., s] * y[..., :].  x: [B, S, n, D] fp16/bf16 CUDA tensor
+    (the streams MhcPre read); y: [B, S, D] in x's dtype (the layer output); hPost
+    [B, S, n] and hRes [B, S, n, n] fp32 from MhcPre.  Returns xNext [B, S, n, D]
+    (out may be x itself: the step runs in place)."""
+    if x.dim() != 4:
+        raise MhcPreError(-2, "x must be 4-D [B, S, n, D]")
+    B, S, n, D = x.shape
+    torch = _torch()
+    if y.dtype != x.dtype:
+        raise MhcPreError(-6, f"y dtype {y.dtype} differs from x dtype {x.dtype}")
+    if tuple(y.shape) != (B, S, D) or tuple(hPost.shape) != (B, S, n) or tuple(hRes.shape) != (B, S, n, n):
+        raise MhcPreError(-2, "y, hPost, hRes shapes must be [B,S,D], [B,S,n], [B,S,n,n]")
+    if hPost.dtype != torch.float32 or hRes.dtype != torch.float32:
+        raise MhcPreError(-6, "hPost and hRes must be fp32")
+    for t in (x, y, hPost, hRes):
+        if not t.is_contiguous():
+            raise MhcPreError(-2, "tensors must be contiguous")
+    if out is None:
+        out = torch.empty_like(x)
+    desc = make_desc(B, S, n, D, _dtype_code(x.dtype), False)
+    _check(lib().mhcPostRun(ctypes.byref(desc), _ptr(x), _ptr(y), _ptr(hPost), _ptr(hRes), _ptr(out),
+                            _stream_ptr(stream)), "PostRun")
+    return out

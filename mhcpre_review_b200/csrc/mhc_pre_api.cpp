@@ -498,6 +498,23 @@ int mhcPreRun(const mhcPreDesc_t* desc, const void* x, const float* phi, const f
     return mhcPreRunPrepared(desc, x, alpha, bias, hIn, hPost, hRes, workspace, workspaceBytes, stream);
 }
 
+int mhcPostRun(const mhcPreDesc_t* desc, const void* x, const void* y, const float* hPost, const float* hRes,
+               void* xNext, void* stream) {
+    Problem p;
+    int rc = make_problem(desc, &p);
+    if (rc != 0) return rc;
+    int sms = 0;
+    rc = device_sm_count(&sms);
+    if (rc != 0) return rc;
+    if (x == nullptr || y == nullptr || hPost == nullptr || hRes == nullptr || xNext == nullptr)
+        return MHC_STATUS_NULL_POINTER;
+    if (!aligned16(x) || !aligned16(y) || !aligned16(xNext) || !aligned4(hPost) || !aligned4(hRes))
+        return MHC_STATUS_MISALIGNED;
+    if (p.M > 0x7fffffff) return MHC_STATUS_TOO_LARGE;  // one block per row
+    const int e = launch_post(p, x, y, hPost, hRes, xNext, static_cast<cudaStream_t>(stream));
+    return e == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
+}
+
 int mhcPreDiagWaitTimeout(uint32_t limitMicroseconds, int32_t* countersGaveUp, int32_t* barriersGaveUp,
                           void* stream) {
     if (countersGaveUp == nullptr || barriersGaveUp == nullptr) return MHC_STATUS_NULL_POINTER;

@@ -95,6 +95,8 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
                const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
                void* workspace, cudaStream_t stream, cudaEvent_t evBegin = nullptr, cudaEvent_t evEnd = nullptr);
 int read_and_clear_device_status(int32_t* status);
+int launch_post(const Problem& p, const void* x, const void* y, const float* hPost, const float* hRes, void* xNext,
+                cudaStream_t stream);
 size_t decode_smem(const Problem& p);  // dynamic shared memory of the decode kernel
 int diag_wait_timeout(uint64_t limit_ns, int* result_host, cudaStream_t stream);
 size_t cluster_extra(const Problem& p);  // cluster kernel's shared memory beyond its rings

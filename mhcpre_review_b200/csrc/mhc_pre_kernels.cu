@@ -561,6 +561,7 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
 #include "mhc_pre_cluster.cuh"
 #include "mhc_pre_decode.cuh"
 #include "mhc_pre_small.cuh"
+#include "mhc_post.cuh"
 
 // ---------------------------------------------------------------------------
 // Launchers
@@ -761,6 +762,35 @@ static int launch_decode(const Problem& p, const Plan& plan, const void* x, cons
 }
 
 size_t decode_smem(const Problem& p) { return decode_smem_bytes(static_cast<int>(p.M), p.mix); }
+
+int launch_post(const Problem& p, const void* x, const void* y, const float* hPost, const float* hRes, void* xNext,
+                cudaStream_t stream) {
+    PostParams pp;
+    pp.M = p.M;
+    pp.D = p.D;
+    pp.x = static_cast<const uint16_t*>(x);
+    pp.y = static_cast<const uint16_t*>(y);
+    pp.hPost = hPost;
+    pp.hRes = hRes;
+    pp.xNext = static_cast<uint16_t*>(xNext);
+    const dim3 grid(static_cast<unsigned>(p.M)), block(kPostThreads);
+    const bool bf = p.dtype == MHC_DTYPE_BF16;
+    switch (p.n) {
+        case 4:
+            if (bf) mhc_post_kernel<MHC_DTYPE_BF16, 4><<<grid, block, 0, stream>>>(pp);
+            else mhc_post_kernel<MHC_DTYPE_F16, 4><<<grid, block, 0, stream>>>(pp);
+            break;
+        case 6:
+            if (bf) mhc_post_kernel<MHC_DTYPE_BF16, 6><<<grid, block, 0, stream>>>(pp);
+            else mhc_post_kernel<MHC_DTYPE_F16, 6><<<grid, block, 0, stream>>>(pp);
+            break;
+        default:
+            if (bf) mhc_post_kernel<MHC_DTYPE_BF16, 8><<<grid, block, 0, stream>>>(pp);
+            else mhc_post_kernel<MHC_DTYPE_F16, 8><<<grid, block, 0, stream>>>(pp);
+            break;
+    }
+    return cudaGetLastError();
+}
 
 template <int DT, int NS>
 static int launch_small_t(const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap, const SmallParams& sp,

@@ -68,6 +68,13 @@ void mhc_oracle_runner_inputs(unsigned seed, int64_t nx, int64_t nphi, int64_t n
 /* Number of OpenMP threads the oracle would use (for reporting). */
 int mhc_oracle_max_threads(void);
 
+/* The mHC post step (mhc_post_oracle.c): xNext[m,s,:] = sum_t hRes[m,s,t]*x[m,t,:]
+ * + hPost[m,s]*y[m,:] in the library's operation order (parity unpinned: the
+ * reference has no such step).  x, y, xNext are 16-bit patterns of the dtype;
+ * xNext must not overlap x or y.  Returns 0, or negative on bad arguments. */
+int mhc_post_oracle(int64_t M, int n, int64_t D, int dtype, const uint16_t *x, const uint16_t *y,
+                    const float *hPost, const float *hRes, uint16_t *xNext, int threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,8 +28,8 @@ DTYPE_CODE = {"fp16": 0, "bf16": 1}
 
 def build(force: bool = False) -> Path:
     """Compile the C oracle in place (gcc + OpenMP)."""
-    src = _HERE / "mhc_pre_oracle.c"
-    if force or not _LIB_PATH.exists() or _LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+    srcs = [_HERE / "mhc_pre_oracle.c", _HERE / "mhc_post_oracle.c", _HERE / "mhc_pre_oracle.h"]
+    if force or not _LIB_PATH.exists() or _LIB_PATH.stat().st_mtime < max(s.stat().st_mtime for s in srcs):
         subprocess.check_call(["make", "-s", "-C", str(_HERE), "libmhc_oracle.so"])
     return _LIB_PATH
 
@@ -58,6 +58,9 @@ def _load():
         lib.mhc_oracle_bf16_to_f32.restype = ctypes.c_float
         lib.mhc_oracle_bf16_to_f32.argtypes = [ctypes.c_uint16]
         lib.mhc_oracle_max_threads.restype = ctypes.c_int
+        lib.mhc_post_oracle.restype = ctypes.c_int
+        lib.mhc_post_oracle.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int64, ctypes.c_int, u16p, u16p,
+                                        f32p, f32p, u16p, ctypes.c_int]
         lib.mhc_oracle_runner_inputs.restype = None
         lib.mhc_oracle_runner_inputs.argtypes = [ctypes.c_uint, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                                  ctypes.c_int64, f32p, f32p, f32p, f32p]
@@ -161,6 +164,36 @@ def mhc_pre_ref(x_bits, phi, alpha, bias, gamma, n: int, D: int, dtype: str,
     if rc != 0:
         raise RuntimeError(f"mhc_pre_oracle failed with code {rc}")
     return hIn[r0:r1], hPost[r0:r1], hRes[r0:r1]
+
+
+def mhc_post_ref(x_bits, y_bits, hPost, hRes, n: int, D: int, dtype: str, threads: int = 0):
+    """The mHC post step in the library's operation order (C oracle; parity
+    unpinned: the reference has no such step).  x_bits: uint16 [M, n, D] (or
+    [M, n*D]); y_bits: uint16 [M, D]; hPost float32 [M, n]; hRes float32 [M, n, n].
+    Returns xNext bits uint16 [M, n, D]."""
+    lib = _load()
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16).reshape(-1, n, D)
+    M = x_bits.shape[0]
+    y_bits = np.ascontiguousarray(y_bits, dtype=np.uint16).reshape(M, D)
+    hPost = np.ascontiguousarray(hPost, dtype=np.float32).reshape(M, n)
+    hRes = np.ascontiguousarray(hRes, dtype=np.float32).reshape(M, n, n)
+    out = np.zeros((M, n, D), dtype=np.uint16)
+    rc = lib.mhc_post_oracle(M, n, D, DTYPE_CODE[dtype], _ptr(x_bits, ctypes.c_uint16), _ptr(y_bits, ctypes.c_uint16),
+                             _ptr(hPost, ctypes.c_float), _ptr(hRes, ctypes.c_float), _ptr(out, ctypes.c_uint16),
+                             threads)
+    if rc != 0:
+        raise RuntimeError(f"mhc_post_oracle failed with code {rc}")
+    return out
+
+
+def mhc_post_numpy(x_bits, y_bits, hPost, hRes, n: int, D: int, dtype: str):
+    """Float64 restatement of the post step (independent of the C oracle's operation
+    order), returned unrounded: float64 [M, n, D]."""
+    x = to_float(np.asarray(x_bits, dtype=np.uint16), dtype).astype(np.float64).reshape(-1, n, D)
+    y = to_float(np.asarray(y_bits, dtype=np.uint16), dtype).astype(np.float64).reshape(x.shape[0], D)
+    hPost = np.asarray(hPost, dtype=np.float64).reshape(-1, n)
+    hRes = np.asarray(hRes, dtype=np.float64).reshape(-1, n, n)
+    return np.einsum("mst,mtd->msd", hRes, x) + hPost[:, :, None] * y[:, None, :]
 
 
 def mhc_pre_numpy(x_bits, phi, alpha, bias, gamma, n: int, D: int, dtype: str,

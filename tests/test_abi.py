@@ -15,7 +15,7 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def declared_symbols():
     text = (ROOT / "include" / "mhc_pre.h").read_text()
-    return sorted(set(re.findall(r"MHC_API\s+[\w\s\*]+?\b(mhcPre\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"MHC_API\s+[\w\s\*]+?\b(mhc(?:Pre|Post)\w+)\s*\(", text)))
 
 
 def test_library_exports_every_declared_symbol():
@@ -49,6 +49,17 @@ def test_rejects_like_reference_tiling(kw, status):
     with pytest.raises(mp.MhcPreError) as ei:
         mp.workspace_size(desc)
     assert ei.value.status == status
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(batch=0), -2), (dict(streams=5), -3), (dict(head_dim=24), -4), (dict(dtype=7), -6),
+])
+def test_post_step_rejects_bad_descriptions_before_the_device(kw, status):
+    args = dict(batch=1, seq=64, streams=4, head_dim=256, dtype=mp.F16)
+    args.update(kw)
+    desc = mp.make_desc(args["batch"], args["seq"], args["streams"], args["head_dim"], args["dtype"], False)
+    assert mp.lib().mhcPostRun(ctypes.byref(desc), None, None, None, None, None, None) == status
+    assert mp.lib().mhcPostRun(None, None, None, None, None, None, None) == -1
 
 
 def test_null_pointers_rejected():
