@@ -1,12 +1,15 @@
-"""MhcPre as a PyTorch custom operator: ``torch.ops.mhc.pre``.
+"""MhcPre and the mHC post step as PyTorch custom operators: ``torch.ops.mhc.pre``
+and ``torch.ops.mhc.post``.
 
-A thin registration over the C ABI (through :func:`mhcpre_review_b200.mhc_pre`), so
-that the operator can sit inside torch code that expects an op: it has a fake
-(meta) implementation giving the output shapes and dtypes, and no autograd (the
-reference operator is forward-only).  Importing this module registers the op.
+Thin registrations over the C ABI (through :func:`mhcpre_review_b200.mhc_pre` and
+:func:`mhcpre_review_b200.mhc_post`), so that the operators can sit inside torch
+code that expects ops: each has a fake (meta) implementation giving the output
+shapes and dtypes, and no autograd (the reference operator is forward-only).
+Importing this module registers both.
 
     import mhcpre_review_b200.torch_ops  # noqa: F401
     hIn, hPost, hRes = torch.ops.mhc.pre(x, phi, alpha, bias, gamma, 1e-6, 1e-6)
+    xNext = torch.ops.mhc.post(x, layer_output, hPost, hRes)
 """
 from __future__ import annotations
 
@@ -15,7 +18,7 @@ from typing import Optional
 import torch
 from torch import Tensor
 
-from . import mhc_pre
+from . import mhc_post, mhc_pre
 
 
 @torch.library.custom_op("mhc::pre", mutates_args=())
@@ -31,3 +34,15 @@ def _pre_fake(x, phi, alpha, bias, gamma=None, norm_eps=1e-6, hc_eps=1e-6):
     B, S, n, D = x.shape
     return (x.new_empty((B, S, D)), x.new_empty((B, S, n), dtype=torch.float32),
             x.new_empty((B, S, n, n), dtype=torch.float32))
+
+
+@torch.library.custom_op("mhc::post", mutates_args=())
+def post(x: Tensor, y: Tensor, hPost: Tensor, hRes: Tensor) -> Tensor:
+    """x [B, S, n, D] fp16/bf16 (the streams); y [B, S, D] in x's dtype (the layer
+    output); hPost [B, S, n] and hRes [B, S, n, n] fp32.  Returns xNext [B, S, n, D]."""
+    return mhc_post(x, y, hPost, hRes)
+
+
+@post.register_fake
+def _post_fake(x, y, hPost, hRes):
+    return x.new_empty(x.shape)

@@ -1,6 +1,6 @@
-"""torch.ops.mhc.pre: the custom-operator registration over the C ABI gives the same
-outputs as the direct binding, and passes torch.library.opcheck (schema, fake
-implementation, dispatch) on the GPU."""
+"""torch.ops.mhc.pre and torch.ops.mhc.post: the custom-operator registrations over
+the C ABI give the same outputs as the direct bindings, and pass
+torch.library.opcheck (schema, fake implementation, dispatch) on the GPU."""
 from __future__ import annotations
 
 import pytest
@@ -28,4 +28,15 @@ def test_torch_op_opcheck():
     inp = make_inputs(cfg)
     torch.library.opcheck(torch.ops.mhc.pre.default,
                           (inp["x"], inp["phi"], inp["alpha"], inp["bias"], inp["gamma"], 1e-6, 1e-6),
+                          test_utils=("test_schema", "test_faketensor"))
+
+
+def test_torch_post_op_matches_binding_and_opcheck():
+    cfg = with_shape(CONFIGS["c2"], seq=64)
+    inp = make_inputs(cfg)
+    hIn, hPost, hRes = mp.mhc_pre(inp["x"], inp["phi"], inp["alpha"], inp["bias"], inp["gamma"])
+    a = torch.ops.mhc.post(inp["x"], hIn, hPost, hRes)
+    b = mp.mhc_post(inp["x"], hIn, hPost, hRes)
+    assert torch.equal(a, b)
+    torch.library.opcheck(torch.ops.mhc.post.default, (inp["x"], hIn, hPost, hRes),
                           test_utils=("test_schema", "test_faketensor"))
