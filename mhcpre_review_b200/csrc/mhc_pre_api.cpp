@@ -57,9 +57,9 @@ static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // At most this many 64-wide chunks per K split for large M (3200 K elements).  At
 // config 4 (448 chunks) that makes 9 splits: 512 tiles x 9 = 4608 items fill 7.8
-// rounds of the GEMM's 592 CTA slots on one GPU, and the 8-GPU shard's 576 items
-// fill 97% of one round (7 splits left the last round almost empty and the shard's
-// round 76% full: 1.5% and 1.4% slower, measured).
+// waves of the GEMM's 592 CTA slots on one GPU, and the 8-GPU shard's 576 items
+// fill 97% of one wave (7 splits left the last wave almost empty and the shard's
+// only wave 76% full: 1.5% and 1.4% slower, measured).
 constexpr int kGroupChunks = 50;
 constexpr int64_t kShardRows = 8192;  // from this M up, splits depend on K only
 constexpr int kMinSplitChunks = 6;    // smallest split below kShardRows rows
