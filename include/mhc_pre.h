@@ -144,7 +144,10 @@ MHC_API int mhcPreRunPreparedProfiled(const mhcPreDesc_t* desc, const void* x, c
  * cudaMalloc, no cudaFree, no allocating library routine.  The first call on a
  * device looks up that device's copy of the array (cudaGetSymbolAddress, which
  * may load the library's device code); make that first call before any stream
- * capture.  All calls on a device share the one array and it keeps the last
+ * capture.  The address is kept for the rest of the process: after
+ * cudaDeviceReset (or any other teardown of the device's primary context) the
+ * library's device code is loaded anew and the kept address is stale, so do not
+ * call this entry point again in that process after a reset.  All calls on a device share the one array and it keeps the last
  * call's contents, so calls that can overlap on the GPU (different streams or
  * host threads without ordering between them) race and corrupt each other:
  * issue them in order, for example on one stream.  No counterpart in the
@@ -168,6 +171,48 @@ typedef struct {
 } mhcPrePlan_t;
 
 MHC_API int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* plan);
+
+/* Plan options: an explicit override of the launch plan, for tests, benchmarks
+ * and profiling.  The entry points above never take options, and the library
+ * reads no environment variables, so their plan depends only on the description
+ * and the device.  In the struct, every field at 0 keeps the library's own choice,
+ * except path, whose default is MHC_PRE_PATH_AUTO.  Options that change the K
+ * splits change the order of the fp32 sums and so the last bits of the results;
+ * the default plan's results are the ones the parity tests pin.  No reference
+ * counterpart (the reference's tiling is fixed by TilingFunc,
+ * code/op_host/mhc_pre.cpp:123-190). */
+#define MHC_PRE_PATH_AUTO (-1)
+typedef struct {
+    int32_t path;          /* MHC_PRE_PATH_AUTO, or a path number of mhcPrePlan_t to use
+                              where it applies: 0 split-K (any shape); 1 fused team
+                              (D % 64 == 0); 2 decode (M <= 32); 3 cluster team
+                              (D/64 a multiple of 8); 4 small batch (M <= 512).  A
+                              path that does not apply falls back to split-K. */
+    int32_t splits;        /* split-K path: K splits */
+    int32_t gemmCtasPerSm; /* split-K path: GEMM CTAs per SM (capped by TMEM and registers) */
+    int32_t gemmStages;    /* split-K path: pipeline depth (2 or more) */
+    int32_t tmaBatch;      /* split-K path: chunks the TMA producer issues per batch */
+    int32_t teamSize;      /* fused team path: CTAs per team (divides D/64, 8..64) */
+    int32_t clusterLead;   /* cluster path: chunks the first read may run ahead of the re-read */
+    int32_t l2Hint;        /* fused and cluster paths: 1 + L2 hint mode (mode 0: none;
+                              1: first read evict_last, re-read evict_first, the default;
+                              2: re-read evict_first only) */
+    int32_t reserved[8];   /* must be 0 */
+} mhcPrePlanOptions_t;
+
+/* mhcPreGetWorkspaceSize / mhcPreQueryPlan / mhcPrePrepareWeights /
+ * mhcPreRunPreparedProfiled under plan options (options may be NULL: the default
+ * plan).  A workspace prepared under one set of options may be run under another
+ * as long as it is large enough for both. */
+MHC_API int mhcPreGetWorkspaceSizeEx(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* options,
+                                     size_t* workspaceBytes);
+MHC_API int mhcPreQueryPlanEx(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* options, mhcPrePlan_t* plan);
+MHC_API int mhcPrePrepareWeightsEx(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* options, const float* phi,
+                                   const float* gamma, void* workspace, size_t workspaceBytes, void* stream);
+MHC_API int mhcPreRunPreparedEx(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* options, const void* x,
+                                const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
+                                void* workspace, size_t workspaceBytes, void* stream, void* mainKernelBegin,
+                                void* mainKernelEnd);
 
 /* Reads and clears the device-side error word of the current device (set when
  * a kernel gave up a bounded wait).  Synchronizes the current device.

@@ -35,7 +35,10 @@ EXPORTED_SYMBOLS = (
     "mhcPreGetWorkspaceSize", "mhcPrePrepareWeights", "mhcPreRun", "mhcPreRunPrepared",
     "mhcPreRunPreparedProfiled", "mhcPreQueryPlan", "mhcPreGetDeviceStatus", "mhcPreStatusString",
     "mhcPreAbiVersion", "mhcPreRunNoAlloc", "mhcPreDiagWaitTimeout", "mhcPostRun",
+    "mhcPreGetWorkspaceSizeEx", "mhcPreQueryPlanEx", "mhcPrePrepareWeightsEx", "mhcPreRunPreparedEx",
 )
+
+PATH_AUTO = -1
 
 
 class MhcPreError(RuntimeError):
@@ -61,6 +64,49 @@ class MhcPrePlan(ctypes.Structure):
                 ("splits", ctypes.c_int32), ("rowsPerTile", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
 
 
+class MhcPrePlanOptions(ctypes.Structure):
+    """mhcPrePlanOptions_t: an explicit override of the launch plan (tests, benchmarks,
+    profiling).  0 keeps the library's choice, except path (PATH_AUTO)."""
+    _fields_ = [("path", ctypes.c_int32), ("splits", ctypes.c_int32), ("gemmCtasPerSm", ctypes.c_int32),
+                ("gemmStages", ctypes.c_int32), ("tmaBatch", ctypes.c_int32), ("teamSize", ctypes.c_int32),
+                ("clusterLead", ctypes.c_int32), ("l2Hint", ctypes.c_int32), ("reserved", ctypes.c_int32 * 8)]
+
+
+def make_plan_options(path=PATH_AUTO, splits=0, gemm_ctas_per_sm=0, gemm_stages=0, tma_batch=0, team_size=0,
+                      cluster_lead=0, l2_hint=0) -> MhcPrePlanOptions:
+    return MhcPrePlanOptions(int(path), int(splits), int(gemm_ctas_per_sm), int(gemm_stages), int(tma_batch),
+                             int(team_size), int(cluster_lead), int(l2_hint))
+
+
+# Plan options every call of this module passes to the library (None: the default
+# plan, which depends only on the description and the device).  Tests and the bench
+# set it, e.g. ``mp._OPTIONS = mp.make_plan_options(path=0)``, or use plan_options().
+_OPTIONS = None
+
+
+class plan_options:
+    """Context manager: ``with plan_options(path=3): ...`` runs the enclosed calls
+    under the given plan options."""
+
+    def __init__(self, **kw):
+        self.opts = make_plan_options(**kw)
+
+    def __enter__(self):
+        global _OPTIONS
+        self.prev = _OPTIONS
+        _OPTIONS = self.opts
+        return self.opts
+
+    def __exit__(self, *exc):
+        global _OPTIONS
+        _OPTIONS = self.prev
+        return False
+
+
+def _opt():
+    return None if _OPTIONS is None else ctypes.byref(_OPTIONS)
+
+
 _lib = None
 
 
@@ -83,6 +129,11 @@ def lib():
         L.mhcPreRunNoAlloc.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
         L.mhcPostRun.argtypes = [dp, vp, vp, vp, vp, vp, vp]
         L.mhcPreGetDeviceStatus.argtypes = [ctypes.POINTER(ctypes.c_int32)]
+        op = ctypes.POINTER(MhcPrePlanOptions)
+        L.mhcPreGetWorkspaceSizeEx.argtypes = [dp, op, ctypes.POINTER(sz)]
+        L.mhcPreQueryPlanEx.argtypes = [dp, op, ctypes.POINTER(MhcPrePlan)]
+        L.mhcPrePrepareWeightsEx.argtypes = [dp, op, vp, vp, vp, sz, vp]
+        L.mhcPreRunPreparedEx.argtypes = [dp, op, vp, vp, vp, vp, vp, vp, vp, sz, vp, vp, vp]
         L.mhcPreStatusString.argtypes = [ctypes.c_int]
         L.mhcPreStatusString.restype = ctypes.c_char_p
         L.mhcPreAbiVersion.argtypes = []
@@ -105,13 +156,13 @@ def make_desc(batch, seq, streams, head_dim, dtype, has_gamma, norm_eps=1e-6, hc
 
 def workspace_size(desc: MhcPreDesc) -> int:
     n = ctypes.c_size_t(0)
-    _check(lib().mhcPreGetWorkspaceSize(ctypes.byref(desc), ctypes.byref(n)), "GetWorkspaceSize")
+    _check(lib().mhcPreGetWorkspaceSizeEx(ctypes.byref(desc), _opt(), ctypes.byref(n)), "GetWorkspaceSize")
     return int(n.value)
 
 
 def query_plan(desc: MhcPreDesc) -> dict:
     p = MhcPrePlan()
-    _check(lib().mhcPreQueryPlan(ctypes.byref(desc), ctypes.byref(p)), "QueryPlan")
+    _check(lib().mhcPreQueryPlanEx(ctypes.byref(desc), _opt(), ctypes.byref(p)), "QueryPlan")
     return {"path": p.path, "kernels_per_run": p.kernelsPerRun, "grid_ctas": p.gridCtas, "splits": p.splits,
             "rows_per_tile": p.rowsPerTile}
 
@@ -151,6 +202,56 @@ def _ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+def _require(t, name, device, dtype=None, shape=None):
+    """Checks one tensor argument before its pointer crosses the C ABI: the kernels
+    read every tensor as dense row-major memory on the device they launch on, so a
+    strided view, a tensor on another GPU, a wrong dtype or a short buffer would be
+    read as something else (or past its end)."""
+    torch = _torch()
+    if not isinstance(t, torch.Tensor):
+        raise MhcPreError(-1, f"{name} must be a torch tensor")
+    if t.device != device:
+        raise MhcPreError(-2, f"{name} is on {t.device}, expected {device}")
+    if not t.is_contiguous():
+        raise MhcPreError(-2, f"{name} must be contiguous")
+    if dtype is not None and t.dtype != dtype:
+        raise MhcPreError(-6, f"{name} dtype {t.dtype}, expected {dtype}")
+    if shape is not None and t.numel() != _numel(shape):
+        raise MhcPreError(-2, f"{name} has {t.numel()} elements, expected {_numel(shape)} ({list(shape)})")
+
+
+def _numel(shape) -> int:
+    n = 1
+    for s in shape:
+        n *= int(s)
+    return n
+
+
+def _check_weights(desc, device, phi, gamma):
+    torch = _torch()
+    K = desc.streams * desc.headDim
+    mix = desc.streams * desc.streams + 2 * desc.streams
+    _require(phi, "phi", device, torch.float32, (mix, K))
+    if bool(desc.hasGamma) != (gamma is not None):
+        raise MhcPreError(-1, "gamma must be given exactly when has_gamma is set")
+    if gamma is not None:
+        _require(gamma, "gamma", device, torch.float32, (desc.streams, desc.headDim))
+
+
+def _check_run(desc, device, x, alpha, bias, out=None):
+    torch = _torch()
+    mix = desc.streams * desc.streams + 2 * desc.streams
+    x_dtype = torch.bfloat16 if desc.dtype == BF16 else torch.float16
+    _require(x, "x", device, x_dtype, (desc.batch, desc.seq, desc.streams, desc.headDim))
+    _require(alpha, "alpha", device, torch.float32, (3,))
+    _require(bias, "bias", device, torch.float32, (mix,))
+    if out is not None:
+        hIn, hPost, hRes = out
+        _require(hIn, "hIn", device, x_dtype, (desc.batch, desc.seq, desc.headDim))
+        _require(hPost, "hPost", device, torch.float32, (desc.batch, desc.seq, desc.streams))
+        _require(hRes, "hRes", device, torch.float32, (desc.batch, desc.seq, desc.streams, desc.streams))
+
+
 def _stream_ptr(stream):
     torch = _torch()
     s = stream if stream is not None else torch.cuda.current_stream()
@@ -165,12 +266,19 @@ class MhcPre:
         torch = _torch()
         self.desc = make_desc(batch, seq, streams, head_dim,
                               dtype if isinstance(dtype, int) else _dtype_code(dtype), has_gamma, norm_eps, hc_eps)
-        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-        self.ws_bytes = workspace_size(self.desc)
+        dev = torch.device("cuda") if device is None else torch.device(device)
+        if dev.type != "cuda":
+            raise MhcPreError(-2, f"device {dev} is not a CUDA device; there is no CPU path")
+        # the plan and the launches use the current device: pin the executor to one
+        self.device = torch.device("cuda", torch.cuda.current_device() if dev.index is None else dev.index)
+        with torch.cuda.device(self.device):
+            self.ws_bytes = workspace_size(self.desc)
         if workspace is None:
             workspace = torch.empty(self.ws_bytes, dtype=torch.uint8, device=self.device)
-        elif workspace.numel() * workspace.element_size() < self.ws_bytes:
-            raise MhcPreError(-8, "workspace")
+        else:
+            _require(workspace, "workspace", self.device)
+            if workspace.numel() * workspace.element_size() < self.ws_bytes:
+                raise MhcPreError(-8, "workspace")
         self.workspace = workspace
         self.prepared = False
 
@@ -179,8 +287,12 @@ class MhcPre:
         return query_plan(self.desc)
 
     def prepare(self, phi, gamma=None, stream=None):
-        _check(lib().mhcPrePrepareWeights(ctypes.byref(self.desc), _ptr(phi), _ptr(gamma), _ptr(self.workspace),
-                                          self.ws_bytes, _stream_ptr(stream)), "PrepareWeights")
+        torch = _torch()
+        _check_weights(self.desc, self.device, phi, gamma)
+        with torch.cuda.device(self.device):
+            _check(lib().mhcPrePrepareWeightsEx(ctypes.byref(self.desc), _opt(), _ptr(phi), _ptr(gamma),
+                                                _ptr(self.workspace), self.ws_bytes, _stream_ptr(stream)),
+                   "PrepareWeights")
         self.prepared = True
 
     def outputs(self, x_dtype):
@@ -193,18 +305,31 @@ class MhcPre:
 
     def run_profiled(self, x, alpha, bias, out, ev_begin, ev_end, stream=None):
         """Like __call__, recording torch.cuda.Event ev_begin/ev_end around the main kernel."""
+        torch = _torch()
+        _check_run(self.desc, self.device, x, alpha, bias, out)
         hIn, hPost, hRes = out
-        _check(lib().mhcPreRunPreparedProfiled(ctypes.byref(self.desc), _ptr(x), _ptr(alpha), _ptr(bias), _ptr(hIn),
-                                               _ptr(hPost), _ptr(hRes), _ptr(self.workspace), self.ws_bytes,
-                                               _stream_ptr(stream), ctypes.c_void_p(ev_begin.cuda_event),
-                                               ctypes.c_void_p(ev_end.cuda_event)), "RunPreparedProfiled")
+        with torch.cuda.device(self.device):
+            _check(lib().mhcPreRunPreparedEx(ctypes.byref(self.desc), _opt(), _ptr(x), _ptr(alpha), _ptr(bias),
+                                             _ptr(hIn), _ptr(hPost), _ptr(hRes), _ptr(self.workspace),
+                                             self.ws_bytes, _stream_ptr(stream),
+                                             ctypes.c_void_p(ev_begin.cuda_event),
+                                             ctypes.c_void_p(ev_end.cuda_event)), "RunPreparedProfiled")
         return hIn, hPost, hRes
 
     def __call__(self, x, alpha, bias, out=None, stream=None):
+        torch = _torch()
+        _check_run(self.desc, self.device, x, alpha, bias, out)
         hIn, hPost, hRes = out if out is not None else self.outputs(x.dtype)
-        _check(lib().mhcPreRunPrepared(ctypes.byref(self.desc), _ptr(x), _ptr(alpha), _ptr(bias), _ptr(hIn),
-                                       _ptr(hPost), _ptr(hRes), _ptr(self.workspace), self.ws_bytes,
-                                       _stream_ptr(stream)), "RunPrepared")
+        with torch.cuda.device(self.device):
+            if _OPTIONS is None:
+                rc = lib().mhcPreRunPrepared(ctypes.byref(self.desc), _ptr(x), _ptr(alpha), _ptr(bias), _ptr(hIn),
+                                             _ptr(hPost), _ptr(hRes), _ptr(self.workspace), self.ws_bytes,
+                                             _stream_ptr(stream))
+            else:
+                rc = lib().mhcPreRunPreparedEx(ctypes.byref(self.desc), _opt(), _ptr(x), _ptr(alpha), _ptr(bias),
+                                               _ptr(hIn), _ptr(hPost), _ptr(hRes), _ptr(self.workspace),
+                                               self.ws_bytes, _stream_ptr(stream), None, None)
+            _check(rc, "RunPrepared")
         return hIn, hPost, hRes
 
 
@@ -213,14 +338,24 @@ def mhc_pre(x, phi, alpha, bias, gamma=None, norm_eps=1e-6, hc_eps=1e-6, out=Non
     phi: fp32 [mix, n*D] (the reference's K-contiguous layout); alpha: fp32 [3];
     bias: fp32 [mix]; gamma: fp32 [n, D] or None.  Returns (hIn [B,S,D], hPost [B,S,n],
     hRes [B,S,n,n])."""
-    if x.dim() != 4:
-        raise MhcPreError(-2, "x must be 4-D [B, S, n, D]")
+    torch = _torch()
+    if not isinstance(x, torch.Tensor) or x.dim() != 4:
+        raise MhcPreError(-2, "x must be a 4-D tensor [B, S, n, D]")
+    if x.device.type != "cuda":
+        raise MhcPreError(-2, f"x must be a CUDA tensor (got {x.device}); there is no CPU path")
     B, S, n, D = x.shape
-    ex = MhcPre(B, S, n, D, x.dtype, gamma is not None, norm_eps, hc_eps, device=x.device, workspace=workspace)
-    hIn, hPost, hRes = out if out is not None else ex.outputs(x.dtype)
-    _check(lib().mhcPreRun(ctypes.byref(ex.desc), _ptr(x), _ptr(phi), _ptr(alpha), _ptr(bias), _ptr(gamma),
-                           _ptr(hIn), _ptr(hPost), _ptr(hRes), _ptr(ex.workspace), ex.ws_bytes,
-                           _stream_ptr(stream)), "Run")
+    with torch.cuda.device(x.device):
+        ex = MhcPre(B, S, n, D, x.dtype, gamma is not None, norm_eps, hc_eps, device=x.device, workspace=workspace)
+        _check_weights(ex.desc, ex.device, phi, gamma)
+        _check_run(ex.desc, ex.device, x, alpha, bias, out)
+        hIn, hPost, hRes = out if out is not None else ex.outputs(x.dtype)
+        if _OPTIONS is None:
+            _check(lib().mhcPreRun(ctypes.byref(ex.desc), _ptr(x), _ptr(phi), _ptr(alpha), _ptr(bias), _ptr(gamma),
+                                   _ptr(hIn), _ptr(hPost), _ptr(hRes), _ptr(ex.workspace), ex.ws_bytes,
+                                   _stream_ptr(stream)), "Run")
+        else:
+            ex.prepare(phi, gamma, stream)
+            ex(x, alpha, bias, out=(hIn, hPost, hRes), stream=stream)
     return hIn, hPost, hRes
 
 
@@ -240,12 +375,15 @@ def mhc_post(x, y, hPost, hRes, out=None, stream=None):
         raise MhcPreError(-2, "y, hPost, hRes shapes must be [B,S,D], [B,S,n], [B,S,n,n]")
     if hPost.dtype != torch.float32 or hRes.dtype != torch.float32:
         raise MhcPreError(-6, "hPost and hRes must be fp32")
-    for t in (x, y, hPost, hRes):
-        if not t.is_contiguous():
-            raise MhcPreError(-2, "tensors must be contiguous")
+    if x.device.type != "cuda":
+        raise MhcPreError(-2, f"x must be a CUDA tensor (got {x.device}); there is no CPU path")
+    for name, t in (("x", x), ("y", y), ("hPost", hPost), ("hRes", hRes)):
+        _require(t, name, x.device)
     if out is None:
         out = torch.empty_like(x)
+    _require(out, "out", x.device, x.dtype, tuple(x.shape))
     desc = make_desc(B, S, n, D, _dtype_code(x.dtype), False)
-    _check(lib().mhcPostRun(ctypes.byref(desc), _ptr(x), _ptr(y), _ptr(hPost), _ptr(hRes), _ptr(out),
-                            _stream_ptr(stream)), "PostRun")
+    with torch.cuda.device(x.device):
+        _check(lib().mhcPostRun(ctypes.byref(desc), _ptr(x), _ptr(y), _ptr(hPost), _ptr(hRes), _ptr(out),
+                                _stream_ptr(stream)), "PostRun")
     return out

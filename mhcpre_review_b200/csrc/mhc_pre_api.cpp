@@ -7,7 +7,6 @@
 // and replaces the Ascend tiling (core split, M64 matmul tiling, tiling cache)
 // with a B200 launch plan.  It keeps no mutable global state.
 #include <algorithm>
-#include <cstdlib>
 #include <cstring>
 
 #include "mhc_pre_internal.h"
@@ -64,7 +63,10 @@ constexpr int kGroupChunks = 50;
 constexpr int64_t kShardRows = 8192;  // from this M up, splits depend on K only
 constexpr int kMinSplitChunks = 6;    // smallest split below kShardRows rows
 
-int make_plan(const Problem& p, int smCount, Plan* plan) {
+int make_plan(const Problem& p, int smCount, const mhcPrePlanOptions_t* opt, Plan* plan) {
+    static const mhcPrePlanOptions_t kDefaults = {MHC_PRE_PATH_AUTO, 0, 0, 0, 0, 0, 0, 0, {0, 0, 0, 0, 0, 0, 0, 0}};
+    const mhcPrePlanOptions_t& o = opt != nullptr ? *opt : kDefaults;
+    const bool autoPath = o.path == MHC_PRE_PATH_AUTO;
     Plan pl{};
     pl.path = 0;
     pl.tilesM = static_cast<int>((p.M + kRowsPerTile - 1) / kRowsPerTile);
@@ -81,8 +83,7 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     const int accCols = accNeed <= 64 ? 64 : accNeed <= 128 ? 128 : accNeed <= 256 ? 256 : 512;
     const int maxCtas = std::min(512 / accCols, p.N <= 48 ? 4 : 2);
     int ctasPerSm = maxCtas;
-    // Tuning override: MHC_PRE_GEMM_CTAS (CTAs per SM, within the limits above).
-    if (const char* ct = std::getenv("MHC_PRE_GEMM_CTAS")) ctasPerSm = std::max(1, std::min(std::atoi(ct), maxCtas));
+    if (o.gemmCtasPerSm > 0) ctasPerSm = std::min(o.gemmCtasPerSm, maxCtas);
     const int slots = ctasPerSm * smCount;
     // K splits.  From kShardRows rows up, the split count depends on K only (groups
     // of at most kGroupChunks chunks), so a row's arithmetic, and therefore its
@@ -94,8 +95,7 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     int splits = groups;
     if (p.M < kShardRows && pl.tilesM < slots)
         splits = std::max(groups, std::min(slots / pl.tilesM, std::max(1, pl.chunks / kMinSplitChunks)));
-    // Tuning override: MHC_PRE_SPLITS (K splits of the split-K path).
-    if (const char* sp = std::getenv("MHC_PRE_SPLITS")) splits = std::max(1, std::atoi(sp));
+    if (o.splits > 0) splits = o.splits;
     splits = std::min(splits, pl.chunks);
     pl.splits = splits;
     const size_t stageBytes = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + static_cast<size_t>(p.N) * kChunk * 2;
@@ -105,9 +105,11 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
                                                                                                         : 55 * 1024;
     int stages = static_cast<int>((budget - fixed) / stageBytes);
     stages = std::max(2, std::min(stages, 8));
-    // Tuning override: MHC_PRE_GEMM_STAGES (ring depth).
-    if (const char* st = std::getenv("MHC_PRE_GEMM_STAGES")) stages = std::max(2, std::min(std::atoi(st), stages));
+    if (o.gemmStages > 0) stages = std::max(2, std::min(o.gemmStages, stages));
     pl.stages = stages;
+    pl.tmaBatch = o.tmaBatch > 0 ? std::min(o.tmaBatch, stages) : std::min(4, stages / 2);
+    pl.l2mode = o.l2Hint > 0 ? std::min(o.l2Hint - 1, 2) : 1;
+    pl.lead = 0;
     pl.gemmGrid = std::min(pl.tilesM * splits, smCount * ctasPerSm);
     pl.smemBytes = fixed + static_cast<size_t>(stages) * stageBytes;
     pl.phiOffset = sizeof(WorkspaceHeader);
@@ -119,11 +121,10 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     // Path 2, the decode kernel, by default for M up to kDecodeDefaultRows: one
     // cooperative launch of one CTA per SM (at most one per 64-wide chunk), CUDA-core
     // partial sums per K-slice, a grid barrier, then the per-row reduction, epilogue
-    // and hIn.  MHC_PRE_PATH=2 selects it up to kDecodeMaxRows (tests); any other
-    // MHC_PRE_PATH value turns it off.
+    // and hIn.  Plan options select it up to kDecodeMaxRows (tests); forcing any
+    // other path turns it off.
     {
-        const char* fp = std::getenv("MHC_PRE_PATH");
-        if ((fp == nullptr && p.M <= kDecodeDefaultRows) || (fp != nullptr && fp[0] == '2' && p.M <= kDecodeMaxRows)) {
+        if ((autoPath && p.M <= kDecodeDefaultRows) || (o.path == 2 && p.M <= kDecodeMaxRows)) {
             pl.path = 2;
             pl.splits = std::min(smCount, pl.chunks);
             pl.gemmGrid = pl.splits;
@@ -143,15 +144,14 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     // runs the tcgen05 contraction of all T = ceil(M/128) row tiles over its K-slice
     // (every tile's MMA reads the same weight chunk); after one grid barrier each CTA
     // reduces the records of its rows (m % G == CTA) and streams their hIn.  It needs
-    // T accumulators of N columns in TMEM.  MHC_PRE_PATH=4 selects it for any M up to
-    // kSmallMaxRows (tests); any other MHC_PRE_PATH value turns it off.  Above
+    // T accumulators of N columns in TMEM.  Plan options select it for any M up to
+    // kSmallMaxRows (tests); forcing any other path turns it off.  Above
     // kSmallDefaultRows rows the split-K path is faster: its epilogue spreads the hIn
     // stream over one CTA per row, while here each SM streams several rows.
     {
-        const char* fp = std::getenv("MHC_PRE_PATH");
-        const bool forced = fp != nullptr && fp[0] == '4';
+        const bool forced = o.path == 4;
         const int tiles = pl.tilesM;
-        if (((fp == nullptr && p.M > kDecodeDefaultRows && p.M <= kSmallDefaultRows) ||
+        if (((autoPath && p.M > kDecodeDefaultRows && p.M <= kSmallDefaultRows) ||
              (forced && p.M <= kSmallMaxRows)) &&
             tiles * p.N <= 512) {
             pl.path = 4;
@@ -171,12 +171,11 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
         }
     }
 
-    // Path 3, the cluster-team kernel (opt-in: MHC_PRE_PATH=3), when D splits into
+    // Path 3, the cluster-team kernel (opt-in through plan options), when D splits into
     // 64-wide chunks evenly over a cluster of S = 16 (or 8) CTAs.  The teams are as
     // many clusters as fit on the device at once.
     {
-        const char* fp = std::getenv("MHC_PRE_PATH");
-        if (fp != nullptr && fp[0] == '3' && p.D % kChunk == 0) {
+        if (o.path == 3 && p.D % kChunk == 0) {
             const int dc = static_cast<int>(p.D / kChunk);
             const int S = dc % 16 == 0 ? 16 : dc % 8 == 0 ? 8 : 0;
             if (S > 0) {
@@ -202,6 +201,7 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
                 c.hpreOffset = c.partOffset;
                 c.cntOffset = c.partOffset;
                 c.cntBytes = 256;  // the global abort word
+                c.lead = o.clusterLead > 0 ? o.clusterLead : c.gStages + 2;
                 c.totalBytes = c.cntOffset + c.cntBytes;
                 int teams = 0;
                 if (c.hStages > 0 && cluster_max_teams(p, c, &teams) == 0 && teams > 0) {
@@ -219,14 +219,12 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
     // teams have in flight fit in L2; S is the smallest divisor that keeps one round
     // of tiles (one per team) under kFusedFootprint among those using the most SMs,
     // else the largest divisor.
-    // It is opt-in (MHC_PRE_PATH=1 in the environment): on B200 one team handshake
+    // It is opt-in (through plan options): on B200 one team handshake
     // (records, owner reduction, hPre) takes tens of microseconds while every SM
     // streams, because each step queues behind the SM's TMA traffic; a byte of x then
     // waits ~80 us for its re-read, far more than L2 holds at full bandwidth, so the
     // re-read mostly misses and the kernel runs slower than the split-K path.
-    const char* force = std::getenv("MHC_PRE_PATH");
-    const bool want1 = force != nullptr && force[0] == '1';
-    if (want1 && p.D % kChunk == 0) {
+    if (o.path == 1 && p.D % kChunk == 0) {
         const int dc = static_cast<int>(p.D / kChunk);
         const double tileBytes = static_cast<double>(kRowsPerTile) * static_cast<double>(p.K) * 2.0;
         constexpr double kFusedFootprint = 40.0e6;
@@ -245,9 +243,9 @@ int make_plan(const Problem& p, int smCount, Plan* plan) {
             for (int S = 8; S <= 64 && S <= smCount; ++S)
                 if (dc % S == 0) bestS = S;
         if (bestS == 0 && dc >= 8 && dc <= 32 && dc <= smCount) bestS = dc;  // owners hold <= 16 rows
-        // MHC_PRE_TEAM=<S> forces the team size (tuning); it must divide D/64, 8 <= S <= 64.
-        if (const char* ts = std::getenv("MHC_PRE_TEAM")) {
-            const int fs = std::atoi(ts);
+        // A team size from the plan options must divide D/64, 8 <= S <= 64.
+        if (o.teamSize > 0) {
+            const int fs = o.teamSize;
             if (fs >= 8 && fs <= 64 && fs <= smCount && dc % fs == 0) bestS = fs;
         }
         if (bestS > 0) {
@@ -330,13 +328,29 @@ static int encode_2d(EncodeTiledFn enc, CUtensorMap* map, const void* base, int 
     return r == CUDA_SUCCESS ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
 }
 
-static int prepare_common(const mhcPreDesc_t* desc, Problem* p, Plan* plan, size_t wsBytes, const void* ws) {
-    int rc = make_problem(desc, p);
+static int options_ok(const mhcPrePlanOptions_t* opt) {
+    if (opt == nullptr) return MHC_STATUS_SUCCESS;
+    if (opt->path < MHC_PRE_PATH_AUTO || opt->path > 4) return MHC_STATUS_BAD_SHAPE;
+    for (int r : opt->reserved)
+        if (r != 0) return MHC_STATUS_BAD_SHAPE;
+    return MHC_STATUS_SUCCESS;
+}
+
+// Validation and plan for the current device under the given options (may be null).
+static int plan_with(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* opt, Problem* p, Plan* plan) {
+    int rc = options_ok(opt);
+    if (rc != 0) return rc;
+    rc = make_problem(desc, p);
     if (rc != 0) return rc;
     int sms = 0;
     rc = device_sm_count(&sms);
     if (rc != 0) return rc;
-    rc = make_plan(*p, sms, plan);
+    return make_plan(*p, sms, opt, plan);
+}
+
+static int prepare_common(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* opt, Problem* p, Plan* plan,
+                          size_t wsBytes, const void* ws) {
+    int rc = plan_with(desc, opt, p, plan);
     if (rc != 0) return rc;
     if (ws == nullptr) return MHC_STATUS_NULL_POINTER;
     if (!aligned16(ws)) return MHC_STATUS_MISALIGNED;
@@ -375,14 +389,7 @@ static int run_prepared(const Problem& p, const Plan& plan, const void* x, const
 // Helpers for the no-allocation entry point (mhc_pre_noalloc.cu): the same
 // validation, plan, weight preparation and launch as the entry points below,
 // with the workspace supplied by the caller of these helpers.
-int plan_for(const mhcPreDesc_t* desc, Problem* p, Plan* plan) {
-    int rc = make_problem(desc, p);
-    if (rc != 0) return rc;
-    int sms = 0;
-    rc = device_sm_count(&sms);
-    if (rc != 0) return rc;
-    return make_plan(*p, sms, plan);
-}
+int plan_for(const mhcPreDesc_t* desc, Problem* p, Plan* plan) { return plan_with(desc, nullptr, p, plan); }
 
 int prepare_and_run(const Problem& p, const Plan& plan, const void* x, const float* phi, const float* alpha,
                     const float* bias, const float* gamma, void* hIn, float* hPost, float* hRes, void* workspace,
@@ -421,31 +428,26 @@ const char* mhcPreStatusString(int status) {
     }
 }
 
-int mhcPreGetWorkspaceSize(const mhcPreDesc_t* desc, size_t* workspaceBytes) {
+int mhcPreGetWorkspaceSizeEx(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* options,
+                             size_t* workspaceBytes) {
     if (workspaceBytes == nullptr) return MHC_STATUS_NULL_POINTER;
     Problem p;
-    int rc = make_problem(desc, &p);
-    if (rc != 0) return rc;
-    int sms = 0;
-    rc = device_sm_count(&sms);
-    if (rc != 0) return rc;
     Plan plan;
-    rc = make_plan(p, sms, &plan);
+    const int rc = plan_with(desc, options, &p, &plan);
     if (rc != 0) return rc;
     *workspaceBytes = plan.totalBytes;
     return MHC_STATUS_SUCCESS;
 }
 
-int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* out) {
+int mhcPreGetWorkspaceSize(const mhcPreDesc_t* desc, size_t* workspaceBytes) {
+    return mhcPreGetWorkspaceSizeEx(desc, nullptr, workspaceBytes);
+}
+
+int mhcPreQueryPlanEx(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* options, mhcPrePlan_t* out) {
     if (out == nullptr) return MHC_STATUS_NULL_POINTER;
     Problem p;
-    int rc = make_problem(desc, &p);
-    if (rc != 0) return rc;
-    int sms = 0;
-    rc = device_sm_count(&sms);
-    if (rc != 0) return rc;
     Plan plan;
-    rc = make_plan(p, sms, &plan);
+    const int rc = plan_with(desc, options, &p, &plan);
     if (rc != 0) return rc;
     std::memset(out, 0, sizeof(*out));
     out->path = plan.path;
@@ -458,11 +460,13 @@ int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* out) {
     return MHC_STATUS_SUCCESS;
 }
 
-int mhcPrePrepareWeights(const mhcPreDesc_t* desc, const float* phi, const float* gamma, void* workspace,
-                         size_t workspaceBytes, void* stream) {
+int mhcPreQueryPlan(const mhcPreDesc_t* desc, mhcPrePlan_t* out) { return mhcPreQueryPlanEx(desc, nullptr, out); }
+
+int mhcPrePrepareWeightsEx(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* options, const float* phi,
+                           const float* gamma, void* workspace, size_t workspaceBytes, void* stream) {
     Problem p;
     Plan plan;
-    int rc = prepare_common(desc, &p, &plan, workspaceBytes, workspace);
+    int rc = prepare_common(desc, options, &p, &plan, workspaceBytes, workspace);
     if (rc != 0) return rc;
     if (phi == nullptr || (p.hasGamma && gamma == nullptr)) return MHC_STATUS_NULL_POINTER;
     if (!aligned4(phi) || (p.hasGamma && !aligned4(gamma))) return MHC_STATUS_MISALIGNED;
@@ -470,24 +474,33 @@ int mhcPrePrepareWeights(const mhcPreDesc_t* desc, const float* phi, const float
     return e == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
 }
 
-int mhcPreRunPrepared(const mhcPreDesc_t* desc, const void* x, const float* alpha, const float* bias, void* hIn,
-                      float* hPost, float* hRes, void* workspace, size_t workspaceBytes, void* stream) {
+int mhcPrePrepareWeights(const mhcPreDesc_t* desc, const float* phi, const float* gamma, void* workspace,
+                         size_t workspaceBytes, void* stream) {
+    return mhcPrePrepareWeightsEx(desc, nullptr, phi, gamma, workspace, workspaceBytes, stream);
+}
+
+int mhcPreRunPreparedEx(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* options, const void* x,
+                        const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes, void* workspace,
+                        size_t workspaceBytes, void* stream, void* mainKernelBegin, void* mainKernelEnd) {
     Problem p;
     Plan plan;
-    int rc = prepare_common(desc, &p, &plan, workspaceBytes, workspace);
+    int rc = prepare_common(desc, options, &p, &plan, workspaceBytes, workspace);
     if (rc != 0) return rc;
-    return run_prepared(p, plan, x, alpha, bias, hIn, hPost, hRes, workspace, static_cast<cudaStream_t>(stream));
+    return run_prepared(p, plan, x, alpha, bias, hIn, hPost, hRes, workspace, static_cast<cudaStream_t>(stream),
+                        static_cast<cudaEvent_t>(mainKernelBegin), static_cast<cudaEvent_t>(mainKernelEnd));
+}
+
+int mhcPreRunPrepared(const mhcPreDesc_t* desc, const void* x, const float* alpha, const float* bias, void* hIn,
+                      float* hPost, float* hRes, void* workspace, size_t workspaceBytes, void* stream) {
+    return mhcPreRunPreparedEx(desc, nullptr, x, alpha, bias, hIn, hPost, hRes, workspace, workspaceBytes, stream,
+                               nullptr, nullptr);
 }
 
 int mhcPreRunPreparedProfiled(const mhcPreDesc_t* desc, const void* x, const float* alpha, const float* bias,
                               void* hIn, float* hPost, float* hRes, void* workspace, size_t workspaceBytes,
                               void* stream, void* mainKernelBegin, void* mainKernelEnd) {
-    Problem p;
-    Plan plan;
-    int rc = prepare_common(desc, &p, &plan, workspaceBytes, workspace);
-    if (rc != 0) return rc;
-    return run_prepared(p, plan, x, alpha, bias, hIn, hPost, hRes, workspace, static_cast<cudaStream_t>(stream),
-                        static_cast<cudaEvent_t>(mainKernelBegin), static_cast<cudaEvent_t>(mainKernelEnd));
+    return mhcPreRunPreparedEx(desc, nullptr, x, alpha, bias, hIn, hPost, hRes, workspace, workspaceBytes, stream,
+                               mainKernelBegin, mainKernelEnd);
 }
 
 int mhcPreRun(const mhcPreDesc_t* desc, const void* x, const float* phi, const float* alpha, const float* bias,

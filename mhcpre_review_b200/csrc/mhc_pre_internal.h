@@ -83,10 +83,16 @@ struct Plan {
     int teamS, teams, J, gStages, hStages;
     size_t hpreOffset, cntOffset, cntBytes;
     size_t totalBytes;
+    // launch tuning (defaults unless plan options override them)
+    int tmaBatch;    // path 0: chunks per TMA producer batch
+    int l2mode;      // paths 1 and 3: L2 hint mode
+    int lead;        // path 3: chunks the first read may run ahead of the re-read
 };
 
 int make_problem(const mhcPreDesc_t* desc, Problem* p);
-int make_plan(const Problem& p, int smCount, Plan* plan);
+// opt may be null (the default plan, which depends on the description and the
+// device only).
+int make_plan(const Problem& p, int smCount, const mhcPrePlanOptions_t* opt, Plan* plan);
 
 // Kernel launchers (return cudaError_t as int).
 int launch_prepare(const Problem& p, const Plan& plan, const float* phi, const float* gamma, void* workspace,
@@ -104,7 +110,7 @@ int cluster_max_teams(const Problem& p, const Plan& plan, int* teams);
 
 // Validation + plan for the current device, and prepare-then-run into a given
 // workspace (used by the no-allocation entry point).
-int plan_for(const mhcPreDesc_t* desc, Problem* p, Plan* plan);
+int plan_for(const mhcPreDesc_t* desc, Problem* p, Plan* plan);  // default plan
 int prepare_and_run(const Problem& p, const Plan& plan, const void* x, const float* phi, const float* alpha,
                     const float* bias, const float* gamma, void* hIn, float* hPost, float* hRes, void* workspace,
                     cudaStream_t stream);

@@ -16,7 +16,6 @@
 // Reference: code/op_kernel/mhc_pre.cpp (the AscendC kernel this replaces).
 #include <algorithm>
 #include <atomic>
-#include <cstdlib>
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -669,10 +668,7 @@ static int launch_fused(const Problem& p, const Plan& plan, const CUtensorMap& x
     fp.W = p.W;
     fp.gStages = plan.gStages;
     fp.hStages = plan.hStages;
-    {
-        const char* hm = std::getenv("MHC_PRE_L2HINT");  // tuning override: 0, 1 or 2
-        fp.l2mode = hm != nullptr ? std::atoi(hm) : 1;
-    }
+    fp.l2mode = plan.l2mode;
     fp.invK = 1.0f / static_cast<float>(p.K);
     fp.normEps = p.normEps;
     fp.hcEps = p.hcEps;
@@ -934,12 +930,8 @@ static int launch_cluster(const Problem& p, const Plan& plan, const CUtensorMap&
     cp.W = p.W;
     cp.gStages = plan.gStages;
     cp.hStages = plan.hStages;
-    {
-        const char* hm = std::getenv("MHC_PRE_L2HINT");  // tuning override: 0, 1 or 2
-        cp.l2mode = hm != nullptr ? std::atoi(hm) : 1;
-        const char* ld = std::getenv("MHC_PRE_LEAD");    // tuning override: chunks
-        cp.lead = ld != nullptr ? std::max(1, std::atoi(ld)) : plan.gStages + 2;
-    }
+    cp.l2mode = plan.l2mode;
+    cp.lead = plan.lead;
     cp.invK = 1.0f / static_cast<float>(p.K);
     cp.normEps = p.normEps;
     cp.hcEps = p.hcEps;
@@ -981,10 +973,7 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
     GemmParams gp;
     gp.M = p.M;
     gp.tilesM = plan.tilesM;
-    {
-        const char* b = std::getenv("MHC_PRE_BATCH");  // tuning override
-        gp.batch = b != nullptr ? std::max(1, std::min(std::atoi(b), plan.stages)) : std::min(4, plan.stages / 2);
-    }
+    gp.batch = std::max(1, plan.tmaBatch);
     gp.mix = p.mix;
     gp.W = p.W;
     gp.chunks = plan.chunks;

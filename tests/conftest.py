@@ -27,3 +27,17 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """With MHC_PARITY_REPORT=<path>, writes the per-case parity statistics the GPU
+    parity tests collected (hIn max ulp and exact-match rate, hPost/hRes max error)
+    as JSON lines."""
+    path = os.environ.get("MHC_PARITY_REPORT")
+    mod = sys.modules.get("tests.test_parity_gpu") or sys.modules.get("test_parity_gpu")
+    if not path or mod is None or not getattr(mod, "PARITY_STATS", None):
+        return
+    import json
+    with open(path, "w") as f:
+        for st in mod.PARITY_STATS:
+            f.write(json.dumps(st) + "\n")

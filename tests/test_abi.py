@@ -97,3 +97,21 @@ def test_algorithmic_bytes_match_baseline_table():
     assert CONFIGS["c4"].algorithmic_bytes() == 4_705_730_668
     assert CONFIGS["c5_m1_g"].algorithmic_bytes() == 2_939_068
     assert CONFIGS["c5_m512_g"].algorithmic_bytes() == 39_608_428
+
+
+def test_plan_options_are_validated_before_the_device():
+    desc = mp.make_desc(1, 64, 4, 256, mp.F16, False)
+    n = ctypes.c_size_t(0)
+    bad = mp.make_plan_options(path=9)
+    assert mp.lib().mhcPreGetWorkspaceSizeEx(ctypes.byref(desc), ctypes.byref(bad), ctypes.byref(n)) == -2
+    bad = mp.make_plan_options()
+    bad.reserved[3] = 1
+    assert mp.lib().mhcPreGetWorkspaceSizeEx(ctypes.byref(desc), ctypes.byref(bad), ctypes.byref(n)) == -2
+
+
+def test_library_reads_no_environment():
+    """The default plan depends only on the description and the device: no source of
+    the library reads environment variables (tuning goes through plan options)."""
+    csrc = ROOT / "mhcpre_review_b200" / "csrc"
+    for f in list(csrc.glob("*.cu")) + list(csrc.glob("*.cuh")) + list(csrc.glob("*.cpp")) + list(csrc.glob("*.h")):
+        assert "getenv" not in f.read_text(), f.name

@@ -1,4 +1,4 @@
-"""The cluster-team single-pass kernel (path 3, MHC_PRE_PATH=3): plan selection,
+"""The cluster-team single-pass kernel (path 3, chosen through plan options): plan selection,
 parity with the CPU oracle on shapes with 16- and 8-CTA clusters (fp16 and bf16,
 n=4/6/8, ragged last tile), agreement with the split-K path, and determinism."""
 from __future__ import annotations
@@ -19,7 +19,7 @@ def _plan(cfg):
 
 
 def test_cluster_plan_for_config4(monkeypatch):
-    monkeypatch.setenv("MHC_PRE_PATH", "3")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=3))
     plan = _plan(CONFIGS["c4"])
     assert plan["path"] == 3 and plan["kernels_per_run"] == 1 and plan["splits"] == 16
     assert plan["grid_ctas"] % 16 == 0 and 16 <= plan["grid_ctas"] <= 148
@@ -36,7 +36,7 @@ CASES = [
 
 @pytest.mark.parametrize("cfg", CASES, ids=lambda c: c.name)
 def test_cluster_parity(cfg, monkeypatch):
-    monkeypatch.setenv("MHC_PRE_PATH", "3")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=3))
     assert _plan(cfg)["path"] == 3
     check_config(cfg)
 
@@ -44,12 +44,12 @@ def test_cluster_parity(cfg, monkeypatch):
 def test_cluster_matches_split_k_and_is_deterministic(monkeypatch):
     cfg = with_shape(CONFIGS["c4"], batch=1, seq=4096)
     inp = make_inputs(cfg)
-    monkeypatch.setenv("MHC_PRE_PATH", "3")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=3))
     a = run_op(inp, use_executor=True)
     b = run_op(inp, use_executor=True)
     for u, v in zip(a, b):
         assert torch.equal(u, v)
-    monkeypatch.setenv("MHC_PRE_PATH", "0")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=0))
     c = run_op(inp, use_executor=True)
     for u, v in zip(a[1:], c[1:]):
         err = (u.double() - v.double()).abs() / v.double().abs().clamp_min(1.0)

@@ -31,7 +31,7 @@ def test_decode_plan(m):
 def test_decode_plan_boundary(monkeypatch):
     base = CONFIGS["c5_m32_g"]
     assert mp.query_plan(_desc(with_shape(base, seq=17)))["path"] == 4  # the small-batch kernel by default
-    monkeypatch.setenv("MHC_PRE_PATH", "2")  # the decode kernel on request, up to 32 rows
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=2))  # the decode kernel on request, up to 32 rows
     assert mp.query_plan(_desc(base))["path"] == 2
     assert mp.query_plan(_desc(with_shape(base, seq=33)))["path"] == 0
 
@@ -50,7 +50,7 @@ CASES = [
 
 @pytest.mark.parametrize("cfg", CASES, ids=lambda c: c.name)
 def test_decode_parity(cfg, monkeypatch):
-    monkeypatch.setenv("MHC_PRE_PATH", "2")  # also above the default range (M <= 16)
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=2))  # also above the default range (M <= 16)
     assert mp.query_plan(_desc(cfg))["path"] == 2
     check_config(cfg)
 
@@ -59,7 +59,7 @@ def test_decode_matches_split_k_path(monkeypatch):
     cfg = CONFIGS["c5_m8_g"]
     inp = make_inputs(cfg)
     dec = run_op(inp, use_executor=True)
-    monkeypatch.setenv("MHC_PRE_PATH", "0")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=0))
     assert mp.query_plan(_desc(cfg))["path"] == 0
     spl = run_op(inp, use_executor=True)
     for a, b in zip(dec[1:], spl[1:]):
@@ -73,7 +73,7 @@ def test_decode_matches_split_k_path(monkeypatch):
 
 
 def test_decode_deterministic_and_repeated_launches(monkeypatch):
-    monkeypatch.setenv("MHC_PRE_PATH", "2")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=2))
     cfg = CONFIGS["c5_m32_ng"]
     inp = make_inputs(cfg)
     x = inp["x"]

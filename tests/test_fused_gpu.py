@@ -1,6 +1,6 @@
 """The fused single-kernel path (path 1): plan selection, parity with the CPU
 oracle on shapes beyond the BASELINE configs, agreement with the split-K path, and
-determinism.  The fused path is opt-in: MHC_PRE_PATH=1 selects it when D is a
+determinism.  The fused path is opt-in: plan options (path=1) select it when D is a
 multiple of 64."""
 from __future__ import annotations
 
@@ -18,7 +18,7 @@ def test_fused_plan_for_config4(monkeypatch):
     cfg = CONFIGS["c4"]
     desc = mp.make_desc(cfg.batch, cfg.seq, cfg.n, cfg.D, mp.BF16, cfg.gamma)
     assert mp.query_plan(desc)["path"] == 0  # the fused kernel is opt-in
-    monkeypatch.setenv("MHC_PRE_PATH", "1")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=1))
     plan = mp.query_plan(desc)
     assert plan["path"] == 1 and plan["kernels_per_run"] == 1
     assert plan["splits"] == 28 and plan["grid_ctas"] == 140  # 5 teams of 28: about 37 MB of tiles in flight
@@ -35,7 +35,7 @@ FORCED = [
 
 @pytest.mark.parametrize("cfg", FORCED, ids=lambda c: c.name)
 def test_fused_parity_forced(cfg, monkeypatch):
-    monkeypatch.setenv("MHC_PRE_PATH", "1")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=1))
     plan = mp.query_plan(mp.make_desc(cfg.batch, cfg.seq, cfg.n, cfg.D, mp.BF16, cfg.gamma))
     assert plan["path"] == 1
     check_config(cfg)
@@ -44,9 +44,9 @@ def test_fused_parity_forced(cfg, monkeypatch):
 def test_fused_and_split_paths_agree(monkeypatch):
     cfg = with_shape(CONFIGS["c4"], batch=1, seq=4096)
     inp = make_inputs(cfg)
-    monkeypatch.setenv("MHC_PRE_PATH", "1")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=1))
     a = run_op(inp)
-    monkeypatch.setenv("MHC_PRE_PATH", "0")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=0))
     b = run_op(inp)
     for name, u, v in (("hPost", a[1], b[1]), ("hRes", a[2], b[2])):
         err = ((u.double() - v.double()).abs() / v.double().abs().clamp_min(1.0)).max().item()

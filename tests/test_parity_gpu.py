@@ -26,8 +26,8 @@ from tests._audit_inputs import audit_inputs, load_golden
 
 pytestmark = pytest.mark.gpu
 
-RTOL = 1e-4
-HIN_BUDGET = 1e-5
+RTOL = ref.RTOL
+PARITY_STATS = []  # per-case statistics of compare(), written out by tests/conftest.py
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
@@ -39,30 +39,11 @@ def np32(t):
 
 
 def compare(got, x_bits, phi, alpha, bias, gamma, n, D, dtype, label="", norm_eps=1e-6, hc_eps=1e-6):
-    """got = (hIn bits [R,D], hPost [R,n], hRes [R,n,n]) for the rows in x_bits."""
-    budget = HIN_BUDGET * max(1.0, n * D / 32768)
-    g_in, g_post, g_res = got
-    r_in, r_post, r_res = ref.mhc_pre_ref(x_bits, phi, alpha, bias, gamma, n, D, dtype, norm_eps, hc_eps)
-    stats = {}
-    for name, g, r in (("hPost", g_post, r_post), ("hRes", g_res, r_res)):
-        err = np.abs(g.astype(np.float64) - r) / np.maximum(1.0, np.abs(r))
-        stats[name] = float(err.max())
-        assert np.all(np.isfinite(g)), f"{label} {name} not finite"
-        assert err.max() <= RTOL, f"{label} {name} max rel err {err.max():.3e}"
-    d = ref.ulp_distance(g_in, r_in)
-    stats["hIn_exact"] = float((d == 0).mean())
-    stats["hIn_max_ulp"] = int(d.max())
-    if (d > 1).any():
-        _, _, _, pre64 = ref.mhc_pre_numpy(x_bits, phi, alpha, bias, gamma, n, D, dtype, norm_eps, hc_eps)
-        xf = ref.to_float(x_bits, dtype).astype(np.float64).reshape(-1, n, D)
-        mag = np.einsum("rs,rsd->rd", np.abs(pre64), np.abs(xf))
-        gf = ref.to_float(g_in, dtype).astype(np.float64)
-        rf = ref.to_float(r_in, dtype).astype(np.float64)
-        ulp = ref.ulp_size(r_in, dtype)
-        ok = np.abs(gf - rf) <= ulp + budget * mag
-        assert ok[d > 1].all(), f"{label} hIn differs beyond 1 ulp without cancellation"
-    if n * D <= 32768:  # beyond, both sides are fp32 approximations: see test_large_head_dims
-        assert stats["hIn_exact"] > 0.99, f"{label} hIn exact-match rate {stats['hIn_exact']}"
+    """got = (hIn bits [R,D], hPost [R,n], hRes [R,n,n]) for the rows in x_bits; the
+    rule is oracle.ref.parity_check (tolerances in this module's docstring).  The
+    statistics are kept for the parity report (tests/conftest.py)."""
+    stats = ref.parity_check(got, x_bits, phi, alpha, bias, gamma, n, D, dtype, label, norm_eps, hc_eps)
+    PARITY_STATS.append(stats)
     return stats
 
 
@@ -89,10 +70,14 @@ def check_config(cfg: Config, sample_rows: int | None = None, seed: int = 0):
         rng = np.random.default_rng(seed)
         rows = np.unique(np.concatenate([np.arange(64), np.arange(M - 64, M),
                                          rng.choice(M, sample_rows, replace=False)]))
-    idx = torch.as_tensor(rows, device="cuda")
-    x_rows = bits(inp["x"].reshape(M, n * D).index_select(0, idx))
-    got = (bits(hIn.reshape(M, D).index_select(0, idx)), hPost.reshape(M, n).index_select(0, idx).cpu().numpy(),
-           hRes.reshape(M, n, n).index_select(0, idx).cpu().numpy())
+    if len(rows) == M:
+        x_rows = bits(inp["x"].reshape(M, n * D))
+        got = (bits(hIn.reshape(M, D)), hPost.reshape(M, n).cpu().numpy(), hRes.reshape(M, n, n).cpu().numpy())
+    else:
+        idx = torch.as_tensor(rows, device="cuda")
+        x_rows = bits(inp["x"].reshape(M, n * D).index_select(0, idx))
+        got = (bits(hIn.reshape(M, D).index_select(0, idx)), hPost.reshape(M, n).index_select(0, idx).cpu().numpy(),
+               hRes.reshape(M, n, n).index_select(0, idx).cpu().numpy())
     gamma = np32(inp["gamma"])
     stats = compare(got, x_rows, np32(inp["phi"]), np32(inp["alpha"]), np32(inp["bias"]),
                     None if gamma is None else gamma.reshape(-1), n, D, cfg.dtype, cfg.name)
@@ -106,8 +91,10 @@ def test_small_configs_all_rows(name):
 
 
 @pytest.mark.parametrize("name", ["c3", "c4"])
-def test_large_configs_sampled_rows(name):
-    check_config(CONFIGS[name], sample_rows=512)
+def test_large_configs_all_rows(name):
+    """Every row of BASELINE configs 3 and 4 against the oracle (a tile-, split- or
+    wave-dependent fault anywhere in the grid shows up)."""
+    check_config(CONFIGS[name])
 
 
 @pytest.mark.parametrize("name", [k for k in CONFIGS if k.startswith("c5_")])
@@ -184,7 +171,7 @@ def test_boundary_shapes(shape):
 def test_boundary_shapes_split_k_path(shape, monkeypatch):
     """The smallest shapes run a single-launch kernel by default; the split-K path
     must handle them too (one 64-wide chunk or a partial one, one ragged row tile)."""
-    monkeypatch.setenv("MHC_PRE_PATH", "0")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=0))
     B, S, n, D, g, dt = shape
     cfg = Config("boundary_splitk", B, S, n, D, dt, 0.05, g, seed=12)
     assert mp.query_plan(mp.make_desc(B, S, n, D, mp.BF16 if dt == "bf16" else mp.F16, g))["path"] == 0

@@ -42,7 +42,7 @@ def test_small_plan_boundaries(monkeypatch):
     # n=8 (N=160): T tiles need T*160 TMEM columns, at most 512: up to 3 tiles
     n8 = Config("n8", 1, 384, 8, 1024, "bf16", 0.01, True)
     assert mp.query_plan(_desc(n8))["path"] == 4
-    monkeypatch.setenv("MHC_PRE_PATH", "4")  # on request up to 512 rows (4 tiles)
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=4))  # on request up to 512 rows (4 tiles)
     assert mp.query_plan(_desc(with_shape(base, seq=1)))["path"] == 4
     assert mp.query_plan(_desc(with_shape(base, seq=512)))["path"] == 4
     assert mp.query_plan(_desc(with_shape(base, seq=513)))["path"] == 0
@@ -67,13 +67,13 @@ CASES = [
 
 @pytest.mark.parametrize("cfg", CASES, ids=lambda c: c.name)
 def test_small_parity(cfg, monkeypatch):
-    monkeypatch.setenv("MHC_PRE_PATH", "4")  # also the 512-row case, above the default range
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=4))  # also the 512-row case, above the default range
     assert mp.query_plan(_desc(cfg))["path"] == 4
     check_config(cfg)
 
 
 def test_small_forced_for_decode_sizes(monkeypatch):
-    monkeypatch.setenv("MHC_PRE_PATH", "4")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=4))
     cfg = CONFIGS["c5_m8_g"]
     assert mp.query_plan(_desc(cfg))["path"] == 4
     check_config(cfg)
@@ -83,10 +83,10 @@ def test_small_forced_for_decode_sizes(monkeypatch):
 def test_small_matches_split_k_path(name, monkeypatch):
     cfg = CONFIGS[name]
     inp = make_inputs(cfg)
-    monkeypatch.setenv("MHC_PRE_PATH", "4")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=4))
     assert mp.query_plan(_desc(cfg))["path"] == 4
     small = run_op(inp, use_executor=True)
-    monkeypatch.setenv("MHC_PRE_PATH", "0")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=0))
     assert mp.query_plan(_desc(cfg))["path"] == 0
     spl = run_op(inp, use_executor=True)
     for a, b in zip(small[1:], spl[1:]):
@@ -122,18 +122,18 @@ def test_small_and_decode_share_the_barrier_counter(monkeypatch):
     cfg = CONFIGS["c5_m32_g"]
     inp = make_inputs(cfg)
     x = inp["x"]
-    monkeypatch.setenv("MHC_PRE_PATH", "4")  # the small-batch plan needs the larger workspace
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=4))  # the small-batch plan needs the larger workspace
     ex = mp.MhcPre(cfg.batch, cfg.seq, cfg.n, cfg.D, x.dtype, cfg.gamma)
     assert ex.plan["path"] == 4
     ex.prepare(inp["phi"], inp["gamma"])
     ref4 = [t.clone() for t in ex(x, inp["alpha"], inp["bias"])]
-    monkeypatch.setenv("MHC_PRE_PATH", "2")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=2))
     assert ex.plan["path"] == 2
     ref2 = [t.clone() for t in ex(x, inp["alpha"], inp["bias"])]
     for _ in range(5):
-        monkeypatch.setenv("MHC_PRE_PATH", "2")
+        monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=2))
         a = [t.clone() for t in ex(x, inp["alpha"], inp["bias"])]
-        monkeypatch.setenv("MHC_PRE_PATH", "4")
+        monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=4))
         b = [t.clone() for t in ex(x, inp["alpha"], inp["bias"])]
         for r, t in zip(ref2, a):
             assert torch.equal(r, t)
@@ -179,7 +179,7 @@ def test_unprepared_workspace_does_not_disturb_the_barrier_counter():
 
 
 def test_small_cuda_graph_replay(monkeypatch):
-    monkeypatch.setenv("MHC_PRE_PATH", "4")
+    monkeypatch.setattr(mp, "_OPTIONS", mp.make_plan_options(path=4))
     cfg = CONFIGS["c5_m512_g"]
     inp = make_inputs(cfg)
     x = inp["x"]
