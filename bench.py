@@ -24,6 +24,12 @@ The JSON line also carries:
                 pinned host x is copied in, the operator runs, hIn/hPost/hRes are
                 copied out (chunked over three streams so copies overlap compute).
   clocks        nvidia-smi samples taken during the timed region.
+  configs_2_3_5 (default one-GPU config-4 run only; --no-extra skips it) the other
+                BASELINE configs measured in the same run, with their own clock
+                samples: configs 2 and 3 (device ms per step, tokens/s, the
+                operator's algorithmic GB/s against the measured copy bandwidth and
+                8 TB/s, the main kernel's fraction), config 5's p50 latencies (as
+                --decode-sweep) and the graph-replay floor of a one-element kernel.
 --impl reference times the reference's own CPU formula (the oracle port; the
 reference itself is AscendC for Ascend 910B and cannot run here) on all host cores.
 
@@ -69,6 +75,13 @@ def parse():
     ap.add_argument("--decode-sweep", action="store_true", help="config 5 latency sweep (its own JSON line)")
     ap.add_argument("--post", action="store_true",
                     help="the mHC post step (mhcPostRun) at the config's shape (its own JSON line, one GPU)")
+    ap.add_argument("--path", type=int, default=-1, help="plan option: force a path (default: the library's)")
+    ap.add_argument("--splits", type=int, default=0, help="plan option: K splits")
+    ap.add_argument("--ctas", type=int, default=0, help="plan option: GEMM CTAs per SM")
+    ap.add_argument("--stages", type=int, default=0, help="plan option: TMA ring depth")
+    ap.add_argument("--ring", type=int, default=0, help="plan option: one-pass record ring slots")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the configs 2, 3 and 5 measurements the default one-GPU run adds to its line")
     ap.add_argument("--no-flush", action="store_true",
                     help="time small shards with a warm L2 (no flush between steps; not a headline number)")
     return ap.parse_args()
@@ -278,7 +291,14 @@ def measure_e2e(mp, inp, cfg, steps, pg, dist, world, total_tokens):
     chunked over rows on three streams so the copies overlap the kernels."""
     import torch
     x = inp["x"]
-    chunks = 8 if cfg.M % 8 == 0 and cfg.M // 8 >= 8192 else 1
+    # chunks of at least 2048 rows, so the H2D copy of one chunk, the operator on the
+    # previous one and the D2H copy of the one before overlap (at 1 to 8 GPUs: 8 chunks
+    # of 8192 / 4096 / 2048 rows, 4 of 2048 at 8 GPUs)
+    chunks = 1
+    for c in (8, 4, 2):
+        if cfg.M % c == 0 and cfg.M // c >= 2048:
+            chunks = c
+            break
     rows = cfg.M // chunks
     xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
     xh.copy_(x)
@@ -391,13 +411,54 @@ def post_step(args):
 
 
 def decode_sweep(args):
-    """p50 latency per M, flushed and unflushed L2."""
+    """p50 latency per M, flushed and unflushed L2 (own JSON line)."""
+    import torch
+    torch.cuda.set_device(0)
+    steps = max(args.steps, 20)
+    results = decode_latencies(args, steps)
+    print(json.dumps({"metric": "MhcPre decode latency (BASELINE config 5)", "unit": "us", "stat": "p50",
+                      "steps": steps, "results": results, "graph_replay_floor": graph_replay_floor()}),
+          flush=True)
+
+
+def graph_replay_floor(reps=200):
+    """p50 time between CUDA events around the replay of a CUDA graph holding one
+    trivial kernel (a one-element add), and around the kernel launched eagerly: the
+    launch floor under the config-5 latencies on this box."""
+    import torch
+    t = torch.zeros(1, device="cuda")
+    for _ in range(10):
+        t.add_(1)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        t.add_(1)
+    out = {}
+    for mode, call in (("graph", graph.replay), ("eager", lambda: t.add_(1))):
+        for _ in range(10):
+            call()
+        ts = []
+        for _ in range(reps):
+            b = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            b.record()
+            call()
+            e.record()
+            torch.cuda.synchronize()
+            ts.append(b.elapsed_time(e) * 1e3)
+        ts.sort()
+        out[f"p50_us_{mode}"] = ts[len(ts) // 2]
+    del graph
+    return out
+
+
+def decode_latencies(args, steps):
+    """Config 5's p50 latencies: M in {1, 8, 32, 128, 512}, gamma on and off; graph
+    replay and eager call, with L2 flushed before every call and warm."""
     import torch
     import mhcpre_review_b200 as mp
     from mhcpre_review_b200.configs import CONFIGS, make_inputs
-    torch.cuda.set_device(0)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-    steps = max(args.steps, 20)
     results = []
     for m in (1, 8, 32, 128, 512):
         for g in (True, False):
@@ -441,8 +502,79 @@ def decode_sweep(args):
             results.append(row)
             if mp.device_status() != 0:
                 raise RuntimeError("device status")
-    print(json.dumps({"metric": "MhcPre decode latency (BASELINE config 5)", "unit": "us", "stat": "p50",
-                      "steps": steps, "results": results}), flush=True)
+    del flush
+    torch.cuda.empty_cache()
+    return results
+
+
+def main_kernel(cfg, plan):
+    """The operator's main kernel for a plan and its algorithmic bytes per launch."""
+    if plan["path"] == 1:
+        return "mhc_pre_fused", cfg.algorithmic_bytes()
+    if plan["path"] == 2:
+        return "mhc_pre_decode", cfg.algorithmic_bytes()
+    if plan["path"] == 3:
+        return "mhc_pre_cluster", cfg.algorithmic_bytes()
+    if plan["path"] == 4:
+        return "mhc_pre_small", cfg.algorithmic_bytes()
+    if plan["path"] == 5:
+        return "mhc_pre_onepass", cfg.algorithmic_bytes()
+    return "gemm_sumsq", cfg.M * cfg.K * 2 + 4 * cfg.K * cfg.mix + (4 * cfg.K if cfg.gamma else 0)
+
+
+def other_configs(args, peak):
+    """BASELINE configs 2 and 3 on this GPU, in the same run as the headline line:
+    device time per step from CUDA events (config 2's x fits in L2, so L2 is flushed
+    with a 256 MB write before each of its steps, outside the step's events; config
+    3's 1.07 GB of x is not), the operator's algorithmic GB/s as a fraction of the
+    measured copy bandwidth and of 8 TB/s, and the main kernel's own fraction."""
+    import torch
+    import mhcpre_review_b200 as mp
+    from mhcpre_review_b200.configs import CONFIGS, make_inputs
+    res = {}
+    steps = max(args.steps, 10)
+    for name in ("c2", "c3"):
+        cfg = CONFIGS[name]
+        inp = make_inputs(cfg)
+        x = inp["x"]
+        ex = mp.MhcPre(cfg.batch, cfg.seq, cfg.n, cfg.D, x.dtype, cfg.gamma, cfg.norm_eps, cfg.hc_eps)
+        ex.prepare(inp["phi"], inp["gamma"])
+        out = ex.outputs(x.dtype)
+        flush = needs_flush(cfg, cfg.M)
+        flush_buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda") if flush else None
+        for _ in range(max(args.warmup, 3)):
+            ex(x, inp["alpha"], inp["bias"], out=out)
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(steps)] for _ in range(4)]
+        for e in ev[2] + ev[3]:
+            e.record()
+        torch.cuda.synchronize()
+        for i in range(steps):
+            if flush:
+                flush_buf.fill_(i & 0xFF)
+            ev[0][i].record()
+            ex.run_profiled(x, inp["alpha"], inp["bias"], out, ev[2][i], ev[3][i])
+            ev[1][i].record()
+        torch.cuda.synchronize()
+        if mp.device_status() != 0:
+            raise RuntimeError(f"device status after {name}")
+        ms = sum(b.elapsed_time(e) for b, e in zip(ev[0], ev[1])) / steps
+        kms = sum(b.elapsed_time(e) for b, e in zip(ev[2], ev[3])) / steps
+        plan = ex.plan
+        kernel, kbytes = main_kernel(cfg, plan)
+        op_gbs = cfg.algorithmic_bytes() / (ms * 1e-3) / 1e9
+        k_gbs = kbytes / (kms * 1e-3) / 1e9
+        res[name] = {
+            "workload": f"M={cfg.M} (B={cfg.batch},S={cfg.seq}), n={cfg.n}, D={cfg.D}, {cfg.dtype}, "
+                        f"gamma {'on' if cfg.gamma else 'off'}",
+            "ms_per_step": ms, "tokens_per_s": cfg.M / (ms * 1e-3), "steps": steps, "plan": plan,
+            "l2": "flushed before every step" if flush else "inputs larger than L2, no flush",
+            "algorithmic_bytes": cfg.algorithmic_bytes(), "op_GBps": op_gbs, "op_frac_of_measured": op_gbs / peak,
+            "op_frac_of_8TBps": op_gbs / 8000.0,
+            "main_kernel": {"kernel": kernel, "launch_ms": kms, "achieved_GBps": k_gbs, "frac": k_gbs / peak,
+                            "algorithmic_bytes_per_launch": kbytes}}
+        del inp, x, ex, out, flush_buf
+        torch.cuda.empty_cache()
+    return res
 
 
 def main():
@@ -477,6 +609,9 @@ def main():
 
     import mhcpre_review_b200 as mp
     from mhcpre_review_b200.configs import make_inputs, with_shape
+    if args.path >= 0 or args.splits or args.ctas or args.stages or args.ring:
+        mp._OPTIONS = mp.make_plan_options(path=args.path, splits=args.splits, gemm_ctas_per_sm=args.ctas,
+                                           gemm_stages=args.stages, ring_tiles=args.ring)
 
     # every rank generates the same batch (same seeds) and keeps its contiguous rows;
     # the weights are replicated
@@ -547,15 +682,7 @@ def main():
     # roofline of the main kernel
     peak, peak_kind = measured_peaks()
     main_avg_ms = sum(main_ms) / len(main_ms)
-    if plan["path"] == 1:
-        kernel, kbytes = "mhc_pre_fused", cfg.algorithmic_bytes()
-    elif plan["path"] == 2:
-        kernel, kbytes = "mhc_pre_decode", cfg.algorithmic_bytes()
-    elif plan["path"] == 4:
-        kernel, kbytes = "mhc_pre_small", cfg.algorithmic_bytes()
-    else:
-        kernel = "gemm_sumsq"
-        kbytes = cfg.M * cfg.K * 2 + 4 * cfg.K * cfg.mix + (4 * cfg.K if cfg.gamma else 0)
+    kernel, kbytes = main_kernel(cfg, plan)
     achieved = kbytes / (main_avg_ms * 1e-3) / 1e9
     op_gbs = cfg.algorithmic_bytes() / (ms_step * 1e-3) / 1e9
     roofline = {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -585,6 +712,19 @@ def main():
                "sample": f"first {rows} of the {cfg.M} rows of {cfg.name} (same inputs), {passes} pass(es), "
                          f"{secs:.1f} s"}
 
+    # BASELINE configs 2, 3 and 5 in the same run (one GPU): their own numbers with
+    # clocks, kept out of the headline value
+    extra = None
+    if world == 1 and not args.no_extra and args.config == "c4" and args.batch == 0:
+        del x, inp
+        torch.cuda.empty_cache()
+        with ClockSampler(local) as xclocks:
+            extra = {"other_configs": other_configs(args, peak),
+                     "c5_decode_latency": {"stat": "p50", "unit": "us",
+                                           "results": decode_latencies(args, max(args.steps, 20)),
+                                           "graph_replay_floor": graph_replay_floor()}}
+        extra["clocks"] = xclocks.summary()
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -595,6 +735,8 @@ def main():
             "gpu_launches": args.steps * plan["kernels_per_run"],
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
         }
+        if extra is not None:
+            line["configs_2_3_5"] = extra
         print(json.dumps(line), flush=True)
     if pg:
         dist.barrier()

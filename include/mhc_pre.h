@@ -162,7 +162,8 @@ typedef struct {
     int32_t path;           /* 0 = split-K GEMM + epilogue kernels, 1 = fused team kernel
                                (opt-in), 2 = single-launch decode kernel (M <= 16),
                                3 = cluster-team kernel (opt-in), 4 = single-launch
-                               small-batch kernel (16 < M <= 384) */
+                               small-batch kernel (16 < M <= 384), 5 = one-pass
+                               kernel (x read from HBM once) */
     int32_t kernelsPerRun;  /* kernels launched by mhcPreRunPrepared */
     int32_t gridCtas;       /* CTAs of the main kernel */
     int32_t splits;         /* K splits (paths 0, 2 and 4) or team size (paths 1 and 3) */
@@ -186,18 +187,21 @@ typedef struct {
     int32_t path;          /* MHC_PRE_PATH_AUTO, or a path number of mhcPrePlan_t to use
                               where it applies: 0 split-K (any shape); 1 fused team
                               (D % 64 == 0); 2 decode (M <= 32); 3 cluster team
-                              (D/64 a multiple of 8); 4 small batch (M <= 512).  A
-                              path that does not apply falls back to split-K. */
-    int32_t splits;        /* split-K path: K splits */
-    int32_t gemmCtasPerSm; /* split-K path: GEMM CTAs per SM (capped by TMEM and registers) */
-    int32_t gemmStages;    /* split-K path: pipeline depth (2 or more) */
-    int32_t tmaBatch;      /* split-K path: chunks the TMA producer issues per batch */
+                              (D/64 a multiple of 8); 4 small batch (M <= 512); 5 one
+                              pass (n = 4).  A path that does not apply falls back to
+                              split-K. */
+    int32_t splits;        /* split-K and one-pass paths: K splits */
+    int32_t gemmCtasPerSm; /* split-K and one-pass paths: GEMM CTAs per SM (capped by
+                              TMEM, registers and shared memory; one pass: 2 or 3) */
+    int32_t gemmStages;    /* split-K and one-pass paths: pipeline depth (2 or more) */
+    int32_t tmaBatch;      /* split-K and one-pass paths: chunks the TMA producer issues per batch */
     int32_t teamSize;      /* fused team path: CTAs per team (divides D/64, 8..64) */
     int32_t clusterLead;   /* cluster path: chunks the first read may run ahead of the re-read */
     int32_t l2Hint;        /* fused and cluster paths: 1 + L2 hint mode (mode 0: none;
                               1: first read evict_last, re-read evict_first, the default;
                               2: re-read evict_first only) */
-    int32_t reserved[8];   /* must be 0 */
+    int32_t ringTiles;     /* one-pass path: tile slots of the partial-record ring */
+    int32_t reserved[7];   /* must be 0 */
 } mhcPrePlanOptions_t;
 
 /* mhcPreGetWorkspaceSize / mhcPreQueryPlan / mhcPrePrepareWeights /

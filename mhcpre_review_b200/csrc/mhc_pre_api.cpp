@@ -64,7 +64,7 @@ constexpr int64_t kShardRows = 8192;  // from this M up, splits depend on K only
 constexpr int kMinSplitChunks = 6;    // smallest split below kShardRows rows
 
 int make_plan(const Problem& p, int smCount, const mhcPrePlanOptions_t* opt, Plan* plan) {
-    static const mhcPrePlanOptions_t kDefaults = {MHC_PRE_PATH_AUTO, 0, 0, 0, 0, 0, 0, 0, {0, 0, 0, 0, 0, 0, 0, 0}};
+    static const mhcPrePlanOptions_t kDefaults = {MHC_PRE_PATH_AUTO, 0, 0, 0, 0, 0, 0, 0, 0, {0, 0, 0, 0, 0, 0, 0}};
     const mhcPrePlanOptions_t& o = opt != nullptr ? *opt : kDefaults;
     const bool autoPath = o.path == MHC_PRE_PATH_AUTO;
     Plan pl{};
@@ -169,6 +169,35 @@ int make_plan(const Problem& p, int smCount, const mhcPrePlanOptions_t* opt, Pla
             *plan = pl;
             return MHC_STATUS_SUCCESS;
         }
+    }
+
+    // Path 5, the one-pass kernel (n = 4; opt-in through plan options): x is read from
+    // HBM once.  Work items of kOnePassItemChunks chunks (a K-split count that depends
+    // on K only, so results never depend on M), three CTAs per SM with four hIn warps
+    // each, or two with eight; the ring depth fills each CTA's share of shared memory.
+    if (o.path == 5 && p.n == 4) {
+        Plan c = pl;
+        c.path = 5;
+        c.opCtasPerSm = o.gemmCtasPerSm == 2 ? 2 : 3;
+        const int groups = c.opCtasPerSm == 2 ? 2 : 1;
+        c.splits = o.splits > 0 ? std::min(o.splits, pl.chunks) : std::max(1, pl.chunks / kOnePassItemChunks);
+        const size_t ctaBudget = c.opCtasPerSm == 2 ? 113 * 1024 : 75 * 1024;
+        int st = static_cast<int>((ctaBudget - onepass_host_smem(stageBytes, 0, groups)) / stageBytes);
+        st = std::max(2, std::min(st, 8));
+        if (o.gemmStages > 0) st = std::max(2, std::min(o.gemmStages, st));
+        c.stages = st;
+        c.tmaBatch = o.tmaBatch > 0 ? std::min(o.tmaBatch, st) : std::max(1, std::min(4, st / 2));
+        c.ringTiles = std::min(o.ringTiles > 0 ? o.ringTiles : kOnePassRingTiles, pl.tilesM);
+        c.gemmGrid = c.opCtasPerSm * smCount;
+        c.smemBytes = onepass_host_smem(stageBytes, st, groups);
+        c.partOffset = align_up(pl.phiOffset + pl.phiBytes, 256);
+        c.partBytes = static_cast<size_t>(c.ringTiles) * kRowsPerTile * static_cast<size_t>(c.splits) *
+                      static_cast<size_t>(p.W) * 4;
+        c.cntOffset = align_up(c.partOffset + c.partBytes, 256);
+        c.cntBytes = align_up((2 * static_cast<size_t>(c.ringTiles) + 1) * 4, 256);
+        c.totalBytes = c.cntOffset + c.cntBytes;
+        *plan = c;
+        return MHC_STATUS_SUCCESS;
     }
 
     // Path 3, the cluster-team kernel (opt-in through plan options), when D splits into
@@ -330,7 +359,7 @@ static int encode_2d(EncodeTiledFn enc, CUtensorMap* map, const void* base, int 
 
 static int options_ok(const mhcPrePlanOptions_t* opt) {
     if (opt == nullptr) return MHC_STATUS_SUCCESS;
-    if (opt->path < MHC_PRE_PATH_AUTO || opt->path > 4) return MHC_STATUS_BAD_SHAPE;
+    if (opt->path < MHC_PRE_PATH_AUTO || opt->path > 5) return MHC_STATUS_BAD_SHAPE;
     for (int r : opt->reserved)
         if (r != 0) return MHC_STATUS_BAD_SHAPE;
     return MHC_STATUS_SUCCESS;
@@ -451,7 +480,7 @@ int mhcPreQueryPlanEx(const mhcPreDesc_t* desc, const mhcPrePlanOptions_t* optio
     if (rc != 0) return rc;
     std::memset(out, 0, sizeof(*out));
     out->path = plan.path;
-    out->kernelsPerRun = plan.path == 0 ? 2 : 1;
+    out->kernelsPerRun = plan.path == 0 ? 2 : 1;  // (the one-pass path also clears its counters: a memset)
     const bool teamPath = plan.path == 1 || plan.path == 3;
     out->gridCtas = teamPath ? plan.teams * plan.teamS : plan.gemmGrid;
     out->splits = teamPath ? plan.teamS : plan.splits;

@@ -87,7 +87,17 @@ struct Plan {
     int tmaBatch;    // path 0: chunks per TMA producer batch
     int l2mode;      // paths 1 and 3: L2 hint mode
     int lead;        // path 3: chunks the first read may run ahead of the re-read
+    // path 5 (one pass): record ring slots and CTAs per SM
+    int ringTiles;
+    int opCtasPerSm;
 };
+
+// One-pass kernel (path 5) layout constants, shared by the plan and the launcher.
+constexpr int kOnePassItemChunks = 4;  // default 64-wide chunks per work item
+constexpr int kOnePassRingTiles = 16;  // default record ring slots
+constexpr size_t onepass_host_smem(size_t stageBytes, int stages, int groups) {
+    return 1024 + static_cast<size_t>(stages) * stageBytes + 256 + static_cast<size_t>(groups) * (4 * 32 + 32) * 4;
+}
 
 int make_problem(const mhcPreDesc_t* desc, Problem* p);
 // opt may be null (the default plan, which depends on the description and the

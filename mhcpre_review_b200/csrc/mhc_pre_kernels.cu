@@ -560,6 +560,7 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
 #include "mhc_pre_cluster.cuh"
 #include "mhc_pre_decode.cuh"
 #include "mhc_pre_small.cuh"
+#include "mhc_pre_onepass.cuh"
 #include "mhc_post.cuh"
 
 // ---------------------------------------------------------------------------
@@ -959,9 +960,85 @@ static int launch_cluster(const Problem& p, const Plan& plan, const CUtensorMap&
     return 0;
 }
 
+template <int DT, int EW, int MINB>
+static int launch_onepass_t(const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
+                            const OnePassParams& op, cudaStream_t stream) {
+    auto kern = mhc_pre_onepass_kernel<DT, 4, EW, MINB>;
+    static std::atomic<int> setBytes[kMaxDevices];
+    cudaError_t e = ensure_smem(kern, setBytes, plan.smemBytes);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 0, occ = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, onepass_threads<EW>(), plan.smemBytes)) !=
+        cudaSuccess)
+        return e;
+    // every CTA must be resident (the hIn warps wait for other CTAs' items): one
+    // cooperative launch of at most the co-resident CTAs (results do not depend on G)
+    const int grid = std::min(plan.gemmGrid, std::max(1, std::min(occ, plan.opCtasPerSm)) * sms);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(onepass_threads<EW>(), 1, 1);
+    cfg.dynamicSmemBytes = plan.smemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, xMap, phiMap, op);
+}
+
+static int launch_onepass(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
+                          const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
+                          void* workspace, cudaStream_t stream, cudaEvent_t evBegin, cudaEvent_t evEnd) {
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaError_t e = cudaMemsetAsync(ws + plan.cntOffset, 0, plan.cntBytes, stream);
+    if (e != cudaSuccess) return e;
+    OnePassParams op;
+    op.M = p.M;
+    op.D = p.D;
+    op.K = p.K;
+    op.tilesM = plan.tilesM;
+    op.chunks = plan.chunks;
+    op.splits = plan.splits;
+    op.stages = plan.stages;
+    op.batch = std::max(1, plan.tmaBatch);
+    op.W = p.W;
+    op.RT = plan.ringTiles;
+    op.invK = 1.0f / static_cast<float>(p.K);
+    op.normEps = p.normEps;
+    op.hcEps = p.hcEps;
+    op.signature = p.signature;
+    op.x = static_cast<const uint16_t*>(x);
+    op.alpha = alpha;
+    op.bias = bias;
+    op.hIn = static_cast<uint16_t*>(hIn);
+    op.hPost = hPost;
+    op.hRes = hRes;
+    op.rec = reinterpret_cast<float*>(ws + plan.partOffset);
+    op.cnt = reinterpret_cast<unsigned*>(ws + plan.cntOffset);
+    op.hdr = reinterpret_cast<const WorkspaceHeader*>(workspace);
+    if (evBegin != nullptr && cudaEventRecord(evBegin, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    const bool bf = p.dtype == MHC_DTYPE_BF16;
+    int rc;
+    if (plan.opCtasPerSm == 2)
+        rc = bf ? launch_onepass_t<MHC_DTYPE_BF16, 8, 2>(plan, xMap, phiMap, op, stream)
+                : launch_onepass_t<MHC_DTYPE_F16, 8, 2>(plan, xMap, phiMap, op, stream);
+    else
+        rc = bf ? launch_onepass_t<MHC_DTYPE_BF16, 4, 3>(plan, xMap, phiMap, op, stream)
+                : launch_onepass_t<MHC_DTYPE_F16, 4, 3>(plan, xMap, phiMap, op, stream);
+    if (rc != 0) return rc;
+    if (evEnd != nullptr && cudaEventRecord(evEnd, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
+    return 0;
+}
+
 int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,
                const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
                void* workspace, cudaStream_t stream, cudaEvent_t evBegin, cudaEvent_t evEnd) {
+    if (plan.path == 5)
+        return launch_onepass(p, plan, xMap, phiMap, x, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin,
+                              evEnd);
     if (plan.path == 1)
         return launch_fused(p, plan, xMap, phiMap, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);
     if (plan.path == 2)
