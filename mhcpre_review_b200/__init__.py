@@ -21,6 +21,8 @@ from pathlib import Path
 
 _PKG = Path(__file__).resolve().parent
 LIB_PATH = _PKG / "libmhcpre_b200.so"
+# the same library built with -DMHC_TRACE: stage stamps, mhcPreTraceRead
+TRACE_LIB_PATH = _PKG / "libmhcpre_b200_trace.so"
 
 F16 = 0
 BF16 = 1
@@ -108,17 +110,19 @@ def _opt():
     return None if _OPTIONS is None else ctypes.byref(_OPTIONS)
 
 
-_lib = None
+_libs = {}
+_lib_path = LIB_PATH
 
 
 def lib():
-    """Loads libmhcpre_b200.so (raises if it has not been built)."""
-    global _lib
-    if _lib is None:
-        if not LIB_PATH.exists():
-            raise RuntimeError(f"{LIB_PATH} is missing: run `python -m mhcpre_review_b200.build` "
+    """Loads libmhcpre_b200.so, or the library selected with use_library (raises if
+    it has not been built)."""
+    L = _libs.get(_lib_path)
+    if L is None:
+        if not _lib_path.exists():
+            raise RuntimeError(f"{_lib_path} is missing: run `python -m mhcpre_review_b200.build` "
                                "(the operator has no CPU fallback)")
-        L = ctypes.CDLL(str(LIB_PATH))
+        L = ctypes.CDLL(str(_lib_path))
         vp, sz = ctypes.c_void_p, ctypes.c_size_t
         dp = ctypes.POINTER(MhcPreDesc)
         L.mhcPreGetWorkspaceSize.argtypes = [dp, ctypes.POINTER(sz)]
@@ -141,8 +145,46 @@ def lib():
         for name in EXPORTED_SYMBOLS:
             if name != "mhcPreStatusString":
                 getattr(L, name).restype = ctypes.c_int
-        _lib = L
-    return _lib
+        if hasattr(L, "mhcPreTraceRead"):
+            L.mhcPreTraceRead.argtypes = [vp, sz, ctypes.POINTER(sz)]
+            L.mhcPreTraceRead.restype = ctypes.c_int
+        _libs[_lib_path] = L
+    return L
+
+
+class use_library:
+    """``with use_library(TRACE_LIB_PATH): ...`` sends the enclosed calls of this
+    module to another build of the library (each keeps its own device state)."""
+
+    def __init__(self, path):
+        self.path = Path(path)
+
+    def __enter__(self):
+        global _lib_path
+        self.prev = _lib_path
+        _lib_path = self.path
+        return lib()
+
+    def __exit__(self, *exc):
+        global _lib_path
+        _lib_path = self.prev
+        return False
+
+
+TRACE_DTYPE = [("t_ns", "<u8"), ("cta", "<u4"), ("warp", "<u2"), ("event", "<u2"), ("a", "<u4"), ("b", "<u4")]
+
+
+def trace_read(max_records: int = 4 << 20):
+    """Reads and clears the stage stamps of the trace build (use inside
+    use_library(TRACE_LIB_PATH)); returns (numpy records, how many were recorded)."""
+    import numpy as np
+    L = lib()
+    if not hasattr(L, "mhcPreTraceRead"):
+        raise RuntimeError("the loaded library is not the trace build")
+    buf = np.zeros(max_records, dtype=TRACE_DTYPE)
+    n = ctypes.c_size_t(0)
+    _check(L.mhcPreTraceRead(ctypes.c_void_p(buf.ctypes.data), max_records, ctypes.byref(n)), "TraceRead")
+    return buf[:min(int(n.value), max_records)], int(n.value)
 
 
 def _check(rc: int, what: str):

@@ -3,6 +3,10 @@
 The library is plain CUDA C++ behind the C ABI in include/mhc_pre.h: no torch
 headers, cudart linked statically, the driver reached through
 cudaGetDriverEntryPoint (so no -lcuda is needed at link time).
+
+``build(trace=True)`` (``python -m mhcpre_review_b200.build --trace``) builds the
+trace library libmhcpre_b200_trace.so instead: the same sources with -DMHC_TRACE,
+which adds the stage stamps and mhcPreTraceRead (include/mhc_pre_trace.h).
 """
 from __future__ import annotations
 
@@ -16,9 +20,10 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libmhcpre_b200.so"
+TRACE_LIB = PKG / "libmhcpre_b200_trace.so"
 SOURCES = ["mhc_pre_kernels.cu", "mhc_pre_api.cpp", "mhc_pre_noalloc.cu"]
 HEADERS = ["ptx.cuh", "mhc_pre_internal.h", "mhc_pre_fused.cuh", "mhc_pre_decode.cuh", "mhc_pre_cluster.cuh",
-           "mhc_pre_small.cuh", "mhc_pre_onepass.cuh", "mhc_post.cuh"]
+           "mhc_pre_small.cuh", "mhc_pre_onepass.cuh", "mhc_post.cuh", "trace.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -33,41 +38,43 @@ def nvcc() -> str:
 
 
 def _inputs():
-    return [CSRC / s for s in SOURCES] + [CSRC / h for h in HEADERS] + [ROOT / "include" / "mhc_pre.h"]
+    return ([CSRC / s for s in SOURCES] + [CSRC / h for h in HEADERS] + [ROOT / "include" / "mhc_pre.h",
+                                                                         ROOT / "include" / "mhc_pre_trace.h"])
 
 
-def needs_build() -> bool:
-    if not LIB.exists():
+def needs_build(lib: Path = LIB) -> bool:
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     return any(p.stat().st_mtime > t for p in _inputs())
 
 
-def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> Path:
-    if not force and not needs_build():
-        return LIB
+def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None, trace: bool = False) -> Path:
+    lib = TRACE_LIB if trace else LIB
+    if not force and not needs_build(lib):
+        return lib
     objs = []
-    build_dir = PKG / "_build"
-    build_dir.mkdir(exist_ok=True)
+    build_dir = PKG / "_build" / ("trace" if trace else "default")
+    build_dir.mkdir(parents=True, exist_ok=True)
+    flags = [*NVCC_FLAGS, *(["-DMHC_TRACE"] if trace else []), *(extra or [])]
     for src in SOURCES:
         obj = build_dir / (Path(src).stem + ".o")
-        cmd = [nvcc(), *NVCC_FLAGS, *(extra or []), "-I", str(ROOT / "include"), "-c", str(CSRC / src), "-o", str(obj)]
+        cmd = [nvcc(), *flags, "-I", str(ROOT / "include"), "-c", str(CSRC / src), "-o", str(obj)]
         if src.endswith(".cpp"):
             cmd[1:1] = ["-x", "cu"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.check_call(cmd)
         objs.append(str(obj))
-    tmp = LIB.with_suffix(".so.tmp")
+    tmp = lib.with_suffix(".so.tmp")
     cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(tmp), *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.check_call(cmd)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    build(force="--force" in sys.argv, verbose=True,
-          extra=["-Xptxas", "-v"] if "--ptxas-v" in sys.argv else None)
-    print(LIB)
+    print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv,
+                extra=["-Xptxas", "-v"] if "--ptxas-v" in sys.argv else None))

@@ -10,6 +10,9 @@
 #include <cstring>
 
 #include "mhc_pre_internal.h"
+#ifdef MHC_TRACE
+#include "../../include/mhc_pre_trace.h"
+#endif
 
 namespace mhc {
 
@@ -179,17 +182,16 @@ int make_plan(const Problem& p, int smCount, const mhcPrePlanOptions_t* opt, Pla
         Plan c = pl;
         c.path = 5;
         c.opCtasPerSm = o.gemmCtasPerSm == 2 ? 2 : 3;
-        const int groups = c.opCtasPerSm == 2 ? 2 : 1;
         c.splits = o.splits > 0 ? std::min(o.splits, pl.chunks) : std::max(1, pl.chunks / kOnePassItemChunks);
         const size_t ctaBudget = c.opCtasPerSm == 2 ? 113 * 1024 : 75 * 1024;
-        int st = static_cast<int>((ctaBudget - onepass_host_smem(stageBytes, 0, groups)) / stageBytes);
+        int st = static_cast<int>((ctaBudget - onepass_host_smem(stageBytes, 0)) / stageBytes);
         st = std::max(2, std::min(st, 8));
         if (o.gemmStages > 0) st = std::max(2, std::min(o.gemmStages, st));
         c.stages = st;
         c.tmaBatch = o.tmaBatch > 0 ? std::min(o.tmaBatch, st) : std::max(1, std::min(4, st / 2));
         c.ringTiles = std::min(o.ringTiles > 0 ? o.ringTiles : kOnePassRingTiles, pl.tilesM);
         c.gemmGrid = c.opCtasPerSm * smCount;
-        c.smemBytes = onepass_host_smem(stageBytes, st, groups);
+        c.smemBytes = onepass_host_smem(stageBytes, st);
         c.partOffset = align_up(pl.phiOffset + pl.phiBytes, 256);
         c.partBytes = static_cast<size_t>(c.ringTiles) * kRowsPerTile * static_cast<size_t>(c.splits) *
                       static_cast<size_t>(p.W) * 4;
@@ -573,6 +575,13 @@ int mhcPreDiagWaitTimeout(uint32_t limitMicroseconds, int32_t* countersGaveUp, i
     *barriersGaveUp = r[1];
     return MHC_STATUS_SUCCESS;
 }
+
+#ifdef MHC_TRACE
+MHC_API int mhcPreTraceRead(void* dst, size_t maxRecords, size_t* recorded) {
+    if (recorded == nullptr) return MHC_STATUS_NULL_POINTER;
+    return trace_read(dst, maxRecords, recorded) == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
+}
+#endif
 
 int mhcPreGetDeviceStatus(int32_t* deviceStatus) {
     if (deviceStatus == nullptr) return MHC_STATUS_NULL_POINTER;

@@ -95,8 +95,8 @@ struct Plan {
 // One-pass kernel (path 5) layout constants, shared by the plan and the launcher.
 constexpr int kOnePassItemChunks = 4;  // default 64-wide chunks per work item
 constexpr int kOnePassRingTiles = 16;  // default record ring slots
-constexpr size_t onepass_host_smem(size_t stageBytes, int stages, int groups) {
-    return 1024 + static_cast<size_t>(stages) * stageBytes + 256 + static_cast<size_t>(groups) * (4 * 32 + 32) * 4;
+constexpr size_t onepass_host_smem(size_t stageBytes, int stages) {
+    return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * stageBytes + 256 /*barriers*/;
 }
 
 int make_problem(const mhcPreDesc_t* desc, Problem* p);
@@ -111,6 +111,7 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
                const void* x, const float* alpha, const float* bias, void* hIn, float* hPost, float* hRes,
                void* workspace, cudaStream_t stream, cudaEvent_t evBegin = nullptr, cudaEvent_t evEnd = nullptr);
 int read_and_clear_device_status(int32_t* status);
+int trace_read(void* dst, size_t maxRecords, size_t* recorded);  // trace build only (MHC_TRACE)
 int launch_post(const Problem& p, const void* x, const void* y, const float* hPost, const float* hRes, void* xNext,
                 cudaStream_t stream);
 size_t decode_smem(const Problem& p);  // dynamic shared memory of the decode kernel

@@ -22,6 +22,7 @@
 
 #include "mhc_pre_internal.h"
 #include "ptx.cuh"
+#include "trace.cuh"
 
 namespace mhc {
 
@@ -248,6 +249,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_min_ctas<N>())
     tc_fence_after();
     // the epilogue grid may start launching now; it waits for this grid in-kernel
     grid_launch_dependents();
+    if (threadIdx.x == 0) MHC_TRACE_EV(kTrKernelBegin, 0, 0);
     const uint32_t tacc = *tmemSlot;
     const bool prepared = p.hdr->magic == kPreparedMagic && p.hdr->signature == p.signature;
     if (!prepared && threadIdx.x == 0) set_device_status(MHC_STATUS_NOT_PREPARED);
@@ -267,6 +269,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_min_ctas<N>())
                 for (int w = blockIdx.x; w < numItems && !*abortFlag; w += G) {
                     int tile, split, cBegin, nChunks;
                     item_range(w, tile, split, cBegin, nChunks);
+                    MHC_TRACE_EV(kTrGemmItemBegin, tile, split);
                     // Chunks are issued in batches of consecutive K ranges, so that each
                     // row's neighbouring 128-byte segments reach DRAM close together.
                     for (int i0 = 0; i0 < nChunks && !*abortFlag; i0 += batch) {
@@ -414,6 +417,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_min_ctas<N>())
                     }
                     out[MIX] = ss;
                 }
+                if (warp == 2 && lane == 0) MHC_TRACE_EV(kTrGemmRecord, tile, split);
             }
             if (!ok && lane == 0) fail();
         }
@@ -426,6 +430,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_min_ctas<N>())
         tc_fence_after();
         tmem_dealloc(tacc, Cfg::kTmemCols);
     }
+    if (threadIdx.x == 0) MHC_TRACE_EV(kTrKernelEnd, 0, 0);
 }
 
 // ---------------------------------------------------------------------------
@@ -480,6 +485,7 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
     const int64_t r = p.M - 1 - blockIdx.x;
     const int tid = threadIdx.x;
     grid_dependency_wait();
+    if (tid == 0) MHC_TRACE_EV(kTrEpiRowBegin, static_cast<uint64_t>(r) & 0xffffffffu, static_cast<uint64_t>(r) >> 32);
     // sum over splits in split order, staged kEpiSplitBlock splits at a time
     float acc = 0.0f;
     for (int sp0 = 0; sp0 < p.splits; sp0 += kEpiSplitBlock) {
@@ -554,6 +560,7 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
         o.w = f32x2_to_x2<DT>(acc[6], acc[7]);
         hr[vi] = o;
     }
+    if (tid == 0) MHC_TRACE_EV(kTrEpiRowDone, static_cast<uint64_t>(r) & 0xffffffffu, static_cast<uint64_t>(r) >> 32);
 }
 
 #include "mhc_pre_fused.cuh"
@@ -1134,6 +1141,25 @@ int diag_wait_timeout(uint64_t limit_ns, int* result_host, cudaStream_t stream) 
     cudaFree(d);
     return e;
 }
+
+#ifdef MHC_TRACE
+// Copies the recorded stage stamps to the host and clears the trace (trace build).
+int trace_read(void* dst, size_t maxRecords, size_t* recorded) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return e;
+    unsigned n = 0;
+    if ((e = cudaMemcpyFromSymbol(&n, g_trace_count, sizeof(n))) != cudaSuccess) return e;
+    const size_t avail = std::min<size_t>(n, kTraceCapacity);
+    const size_t take = std::min(avail, maxRecords);
+    if (take > 0 && dst != nullptr &&
+        (e = cudaMemcpyFromSymbol(dst, g_trace, take * sizeof(TraceRecord))) != cudaSuccess)
+        return e;
+    const unsigned zero = 0;
+    if ((e = cudaMemcpyToSymbol(g_trace_count, &zero, sizeof(zero))) != cudaSuccess) return e;
+    *recorded = n;
+    return 0;
+}
+#endif
 
 int read_and_clear_device_status(int32_t* status) {
     int v = 0;

@@ -9,12 +9,13 @@
 //                   chunks) in tile-major order, item w on CTA w mod G.  An item's
 //                   partial records go into a ring of RT tile slots [slot][row][split][W]
 //                   and add one arrival per warp to the slot's counter.
-//   hIn warps 6..   rows r = b, b + G, ... of CTA b, in groups of four warps (a group per
-//                   row).  For each row: wait for its tile's arrivals; sum its records
-//                   over the splits in a fixed order (four contiguous quarters, then the
-//                   quarters in order); compute invRms, hPre, hPost, hRes in the
-//                   reference's operation order; mark the row's records consumed; then
-//                   re-read the row's x and write hIn.
+//   hIn warps 6..   one row per warp at a time (warp e of CTA b takes rows b + G*e,
+//                   b + G*(e + EW), ...).  For each row: wait for its tile's arrivals;
+//                   sum its records over the splits in split order (lane j, column j);
+//                   mark the row's records consumed; compute invRms, hPre, hPost, hRes
+//                   in the reference's operation order; then re-read the row's x and
+//                   write hIn.  Rows are independent, so the warps of an SM overlap one
+//                   row's records with another's x stream.
 // Items are small (a few chunks), so every tile's items run at about the same time
 // on many CTAs and a tile completes a few microseconds after its first chunk was
 // read: its re-read then finds x in L2, and DRAM sees x once.  The TMA producer does
@@ -82,13 +83,6 @@ __device__ __forceinline__ void add_segment_g(uint32_t lane_base, uint32_t col, 
     }
 }
 
-// Dynamic shared memory: the ring, its barriers, and the hIn groups' quarter sums
-// and hPre.
-template <int N>
-constexpr size_t onepass_smem_bytes(int stages, int groups) {
-    return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * GemmCfg<N>::kStageBytes + 256 /*barriers*/ +
-           static_cast<size_t>(groups) * (4 * 32 + 32) * sizeof(float);
-}
 
 template <int DT, int NS, int EW, int MINB>
 __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
@@ -96,12 +90,10 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
                            const OnePassParams p) {
     constexpr int MIX = NS * NS + 2 * NS;
     constexpr int N = 2 * MIX;
-    constexpr int EG = EW / 4;  // hIn groups of four warps
-    static_assert(EW % 4 == 0 && EW >= 4, "hIn warps come in groups of four");
+    static_assert(EW >= 1, "at least one hIn warp");
     static_assert(MIX + 1 <= 32, "one lane per record column");
     using Cfg = GemmCfg<N>;
     constexpr int kAccBufs = Cfg::kAccBufs;
-    constexpr int kFlushLag = Cfg::kFlushLag;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages;
@@ -111,8 +103,6 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
     uint64_t* accEmpty = accFull + kAccBufs;  // [kAccBufs]
     uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(accEmpty + kAccBufs);
     volatile int* abortFlag = reinterpret_cast<volatile int*>(tmemSlot + 1);
-    float* sQuart = reinterpret_cast<float*>(smem + static_cast<size_t>(S) * Cfg::kStageBytes + 256);  // [EG][4][32]
-    float* sPreAll = sQuart + EG * 4 * 32;                                                            // [EG][32]
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -154,6 +144,7 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (threadIdx.x == 0) MHC_TRACE_EV(kTrKernelBegin, 5, 0);
     const uint32_t tacc = *tmemSlot;
     const bool prepared = p.hdr->magic == kPreparedMagic && p.hdr->signature == p.signature;
     if (!prepared && threadIdx.x == 0) set_device_status(MHC_STATUS_NOT_PREPARED);
@@ -175,11 +166,13 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
                 for (int w = blockIdx.x; w < numItems && !*abortFlag; w += G) {
                     int tile, split, cBegin, nChunks;
                     item_range(w, tile, split, cBegin, nChunks);
+                    MHC_TRACE_EV(kTrGemmItemBegin, tile, split);
                     // the ring slot's previous tile must be consumed (bounds the footprint)
                     if (tile >= p.RT && !wait_counter(&cntDone[tile % p.RT], slot_free_target(tile), gAbort)) {
                         fail();
                         break;
                     }
+                    MHC_TRACE_EV(kTrGemmItemIssue, tile, split);
                     for (int i0 = 0; i0 < nChunks && !*abortFlag; i0 += batch) {
                         const int nb = min(batch, nChunks - i0);
                         bool okb = true;
@@ -268,13 +261,52 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
                 return true;
             };
             const float unscale = ldexpf(1.0f, -p.hdr->phiScaleExp);
-            int g = 0, segBase = 0;
-            bool ok = true;
+            // Each finished accumulator segment is added into run[] one segment later
+            // (when the next one ends, by then long complete), also across items; the
+            // item's record is written when its last segment has been added.
+            int g = 0, gseg = 0;
+            bool ok = true, havePrev = false, prevLast = false;
+            int prevSeg = 0, prevTile = 0, prevSplit = 0;
+            float prevSs = 0.0f;
+#pragma unroll
+            for (int j = 0; j < MIX; ++j) run[j] = 0.0f;
+            auto retire_prev = [&]() -> bool {
+                if (!flush(prevSeg)) return false;
+                if (!prevLast) return true;
+                const int slot = prevTile % p.RT;
+                // the slot's previous tile was consumed before the producer started
+                // this item; checked again where the records are written (bounded)
+                if (prevTile >= p.RT) {
+                    bool freed = true;
+                    if (lane == 0) freed = wait_counter(&cntDone[slot], slot_free_target(prevTile), gAbort);
+                    if (!__shfl_sync(0xffffffffu, freed ? 1 : 0, 0)) return false;
+                }
+                const int64_t grow = static_cast<int64_t>(prevTile) * kRowsPerTile + row;
+                if (grow < p.M) {
+                    float* out =
+                        p.rec + ((static_cast<int64_t>(slot) * kRowsPerTile + row) * p.splits + prevSplit) * p.W;
+#pragma unroll
+                    for (int j0 = 0; j0 < MIX; j0 += 4) {
+                        float4 a;
+                        a.x = __fmul_rn(run[j0 + 0], unscale);
+                        a.y = __fmul_rn(run[j0 + 1], unscale);
+                        a.z = __fmul_rn(run[j0 + 2], unscale);
+                        a.w = __fmul_rn(run[j0 + 3], unscale);
+                        *reinterpret_cast<float4*>(out + j0) = a;
+                    }
+                    out[MIX] = prevSs;
+                }
+#pragma unroll
+                for (int j = 0; j < MIX; ++j) run[j] = 0.0f;
+                // publish: the warp's stores, then one release (cumulative over them)
+                __syncwarp();
+                if (lane == 0) red_release_add(&cntRec[slot], 1u);
+                if (warp == 2 && lane == 0) MHC_TRACE_EV(kTrGemmRecord, prevTile, prevSplit);
+                return true;
+            };
             for (int w = blockIdx.x; w < numItems && ok; w += G) {
                 int tile, split, cBegin, nChunks;
                 item_range(w, tile, split, cBegin, nChunks);
-#pragma unroll
-                for (int j = 0; j < MIX; ++j) run[j] = 0.0f;
                 float ss = 0.0f;
                 for (int i = 0; i < nChunks; ++i, ++g) {
                     const int s = g % S;
@@ -298,163 +330,128 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
                     ss += part;
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[s]);
-                    const int segL = i / kSegChunks;
-                    if ((i % kSegChunks == kSegChunks - 1 || i == nChunks - 1) && segL >= kFlushLag) {
-                        if (!flush(segBase + segL - kFlushLag)) {
+                    if (i % kSegChunks == kSegChunks - 1 || i == nChunks - 1) {
+                        if (havePrev && !retire_prev()) {
                             ok = false;
                             break;
                         }
+                        havePrev = true;
+                        prevSeg = gseg++;
+                        prevLast = i == nChunks - 1;
+                        prevTile = tile;
+                        prevSplit = split;
+                        prevSs = ss;
                     }
                 }
-                {
-                    const int nSeg = (nChunks + kSegChunks - 1) / kSegChunks;
-                    for (int sg = max(0, nSeg - kFlushLag); sg < nSeg && ok; ++sg) ok = flush(segBase + sg);
-                }
-                segBase += (nChunks + kSegChunks - 1) / kSegChunks;
-                if (!ok) break;
-                const int slot = tile % p.RT;
-                // the slot's previous tile was consumed before the producer started this
-                // item; checked again here, where the records are written (bounded)
-                if (tile >= p.RT) {
-                    bool freed = true;
-                    if (lane == 0) freed = wait_counter(&cntDone[slot], slot_free_target(tile), gAbort);
-                    if (!__shfl_sync(0xffffffffu, freed ? 1 : 0, 0)) {
-                        ok = false;
-                        break;
-                    }
-                }
-                const int64_t grow = static_cast<int64_t>(tile) * kRowsPerTile + row;
-                if (grow < p.M) {
-                    float* out = p.rec + ((static_cast<int64_t>(slot) * kRowsPerTile + row) * p.splits + split) * p.W;
-#pragma unroll
-                    for (int j0 = 0; j0 < MIX; j0 += 4) {
-                        float4 a;
-                        a.x = __fmul_rn(run[j0 + 0], unscale);
-                        a.y = __fmul_rn(run[j0 + 1], unscale);
-                        a.z = __fmul_rn(run[j0 + 2], unscale);
-                        a.w = __fmul_rn(run[j0 + 3], unscale);
-                        *reinterpret_cast<float4*>(out + j0) = a;
-                    }
-                    out[MIX] = ss;
-                }
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) red_release_add(&cntRec[slot], 1u);
             }
+            if (ok && havePrev) ok = retire_prev();
             if (!ok && lane == 0) fail();
         } else {
-            // ---------------- hIn groups ----------------
-            const int ew = warp - kOpGemmWarps;  // 0 .. EW-1
-            const int grp = ew >> 2;             // group of four warps
-            const int qw = ew & 3;               // quarter of the splits this warp sums
-            const int gt = qw * 32 + lane;       // thread index within the group
-            const uint32_t barId = 2 + grp;      // named barrier of the group (0: __syncthreads, 1: unused)
-            float* sQ = sQuart + grp * 4 * 32;
-            float* sPre = sPreAll + grp * 32;
+            // ---------------- hIn warps: one row per warp ----------------
+            const int ew = warp - kOpGemmWarps;
             const float a0 = __ldg(p.alpha + 0), a1 = __ldg(p.alpha + 1), a2 = __ldg(p.alpha + 2);
             const float biasL = lane < MIX ? __ldg(p.bias + lane) : 0.0f;
             const unsigned arrivalsPerTile = 4u * static_cast<unsigned>(p.splits);
-            const int spBegin = (qw * p.splits) / 4;
-            const int spEnd = ((qw + 1) * p.splits) / 4;
             const int64_t vecPerStream = p.D / 8;
-            for (int64_t r = blockIdx.x + static_cast<int64_t>(grp) * G; r < p.M; r += static_cast<int64_t>(EG) * G) {
+            const int64_t rowStep = static_cast<int64_t>(G) * EW;
+            for (int64_t r = blockIdx.x + static_cast<int64_t>(ew) * G; r < p.M; r += rowStep) {
                 const int tile = static_cast<int>(r / kRowsPerTile);
                 const int lrow = static_cast<int>(r - static_cast<int64_t>(tile) * kRowsPerTile);
                 const int slot = tile % p.RT;
+                const uint32_t rlo = static_cast<uint32_t>(static_cast<uint64_t>(r) & 0xffffffffu);
+                const uint32_t rhi = static_cast<uint32_t>(static_cast<uint64_t>(r) >> 32);
                 bool ok = true;
-                if (gt == 0)
+                if (lane == 0) {
+                    MHC_TRACE_EV(kTrRowWait, rlo, rhi);
                     ok = wait_counter(&cntRec[slot], arrivalsPerTile * static_cast<unsigned>(tile / p.RT + 1), gAbort);
-                if (bar_red_or(barId, 128, !ok)) {
-                    if (gt == 0) fail();
+                    MHC_TRACE_EV(kTrRowReady, rlo, rhi);
+                }
+                if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+                    if (lane == 0) fail();
                     break;
                 }
-                // this warp's quarter of the splits, lanes over the record's columns
-                {
-                    const float* recRow = p.rec + (static_cast<int64_t>(slot) * kRowsPerTile + lrow) * p.splits * p.W;
-                    float acc = 0.0f;
-                    if (lane <= MIX) {
-                        int sp = spBegin;
-                        for (; sp + 4 <= spEnd; sp += 4) {
-                            const float v0 = __ldcg(recRow + (sp + 0) * p.W + lane);
-                            const float v1 = __ldcg(recRow + (sp + 1) * p.W + lane);
-                            const float v2 = __ldcg(recRow + (sp + 2) * p.W + lane);
-                            const float v3 = __ldcg(recRow + (sp + 3) * p.W + lane);
-                            acc = __fadd_rn(acc, v0);
-                            acc = __fadd_rn(acc, v1);
-                            acc = __fadd_rn(acc, v2);
-                            acc = __fadd_rn(acc, v3);
-                        }
-                        for (; sp < spEnd; ++sp) acc = __fadd_rn(acc, __ldcg(recRow + sp * p.W + lane));
+                // lane j sums record column j over the splits, in split order
+                float acc = 0.0f;
+                if (lane <= MIX) {
+                    const float* col = p.rec + (static_cast<int64_t>(slot) * kRowsPerTile + lrow) * p.splits * p.W + lane;
+                    constexpr int kB = 28;  // loads in flight per lane
+                    int sp = 0;
+                    for (; sp + kB <= p.splits; sp += kB) {
+                        float v[kB];
+#pragma unroll
+                        for (int u = 0; u < kB; ++u) v[u] = __ldcg(col + (sp + u) * p.W);
+#pragma unroll
+                        for (int u = 0; u < kB; ++u) acc = __fadd_rn(acc, v[u]);
                     }
-                    sQ[qw * 32 + lane] = acc;
+                    for (; sp < p.splits; ++sp) acc = __fadd_rn(acc, __ldcg(col + sp * p.W));
                 }
-                named_bar_sync(barId, 128);
-                if (qw == 0) {
-                    // the records of this row are consumed: the slot may be reused
-                    if (lane == 0) red_release_add(&cntDone[slot], 1u);
-                    float v = 0.0f;
-                    if (lane <= MIX)
-                        v = __fadd_rn(__fadd_rn(__fadd_rn(sQ[lane], sQ[32 + lane]), sQ[64 + lane]), sQ[96 + lane]);
-                    const float ssum = __shfl_sync(0xffffffffu, v, MIX);
-                    // invRms = 1 / Sqrt(sum * invFlatDim + normEps)   (mhc_pre.cpp:504-519)
-                    float t = __fmul_rn(ssum, p.invK);
-                    t = __fadd_rn(t, p.normEps);
-                    const float invRms = __fdiv_rn(1.0f, __fsqrt_rn(t));
-                    if (lane < NS) {
-                        const float u = __fadd_rn(__fmul_rn(v, __fmul_rn(invRms, a0)), biasL);
-                        sPre[lane] = __fadd_rn(sigmoid_ref(u), p.hcEps);
-                    } else if (lane < 2 * NS) {
-                        const float u = __fadd_rn(__fmul_rn(v, __fmul_rn(invRms, a1)), biasL);
-                        p.hPost[r * NS + (lane - NS)] = __fmul_rn(sigmoid_ref(u), 2.0f);
-                    } else if (lane < MIX) {
-                        p.hRes[r * NS * NS + (lane - 2 * NS)] = __fadd_rn(__fmul_rn(v, __fmul_rn(invRms, a2)), biasL);
-                    }
+                // every lane's loads have returned (their values are summed): the row's
+                // records are consumed and the slot may be reused
+                __syncwarp();
+                if (lane == 0) {
+                    red_release_add(&cntDone[slot], 1u);
+                    MHC_TRACE_EV(kTrRowReduced, rlo, rhi);
                 }
-                named_bar_sync(barId, 128);
+                const float ssum = __shfl_sync(0xffffffffu, acc, MIX);
+                // invRms = 1 / Sqrt(sum * invFlatDim + normEps)   (mhc_pre.cpp:504-519)
+                float tv = __fmul_rn(ssum, p.invK);
+                tv = __fadd_rn(tv, p.normEps);
+                const float invRms = __fdiv_rn(1.0f, __fsqrt_rn(tv));
+                float hpre = 0.0f;
+                if (lane < NS) {
+                    const float u = __fadd_rn(__fmul_rn(acc, __fmul_rn(invRms, a0)), biasL);
+                    hpre = __fadd_rn(sigmoid_ref(u), p.hcEps);
+                } else if (lane < 2 * NS) {
+                    const float u = __fadd_rn(__fmul_rn(acc, __fmul_rn(invRms, a1)), biasL);
+                    p.hPost[r * NS + (lane - NS)] = __fmul_rn(sigmoid_ref(u), 2.0f);
+                } else if (lane < MIX) {
+                    p.hRes[r * NS * NS + (lane - 2 * NS)] = __fadd_rn(__fmul_rn(acc, __fmul_rn(invRms, a2)), biasL);
+                }
                 float pre[NS];
 #pragma unroll
-                for (int s = 0; s < NS; ++s) pre[s] = sPre[s];
+                for (int s = 0; s < NS; ++s) pre[s] = __shfl_sync(0xffffffffu, hpre, s);
                 // hIn = sum_s hPre[s] * x[s, :], streams in order, separate multiply and
                 // add (mhc_pre.cpp:91-222), rounded to the x dtype (:811-812)
                 const uint4* xr = reinterpret_cast<const uint4*>(p.x + r * p.K);
                 uint4* hr = reinterpret_cast<uint4*>(p.hIn + r * p.D);
-                for (int64_t vi = gt; vi < vecPerStream; vi += 2 * 128) {
-                    const bool two = vi + 128 < vecPerStream;
+                for (int64_t vi = lane; vi < vecPerStream; vi += 64) {
+                    const bool two = vi + 32 < vecPerStream;
                     uint4 wa[NS], wb[NS];
 #pragma unroll
                     for (int s = 0; s < NS; ++s) wa[s] = __ldcs(xr + s * vecPerStream + vi);
                     if (two) {
 #pragma unroll
-                        for (int s = 0; s < NS; ++s) wb[s] = __ldcs(xr + s * vecPerStream + vi + 128);
+                        for (int s = 0; s < NS; ++s) wb[s] = __ldcs(xr + s * vecPerStream + vi + 32);
                     }
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         if (h == 1 && !two) break;
-                        const uint4* w = h == 0 ? wa : wb;
-                        float acc[8];
+                        const uint4* wv = h == 0 ? wa : wb;
+                        float o8[8];
 #pragma unroll
                         for (int s = 0; s < NS; ++s) {
-                            const uint32_t ws[4] = {w[s].x, w[s].y, w[s].z, w[s].w};
+                            const uint32_t ws[4] = {wv[s].x, wv[s].y, wv[s].z, wv[s].w};
 #pragma unroll
                             for (int t = 0; t < 4; ++t) {
                                 const float2 f = x2_to_f32<DT>(ws[t]);
                                 if (s == 0) {
-                                    acc[2 * t] = __fmul_rn(f.x, pre[0]);
-                                    acc[2 * t + 1] = __fmul_rn(f.y, pre[0]);
+                                    o8[2 * t] = __fmul_rn(f.x, pre[0]);
+                                    o8[2 * t + 1] = __fmul_rn(f.y, pre[0]);
                                 } else {
-                                    acc[2 * t] = __fadd_rn(acc[2 * t], __fmul_rn(f.x, pre[s]));
-                                    acc[2 * t + 1] = __fadd_rn(acc[2 * t + 1], __fmul_rn(f.y, pre[s]));
+                                    o8[2 * t] = __fadd_rn(o8[2 * t], __fmul_rn(f.x, pre[s]));
+                                    o8[2 * t + 1] = __fadd_rn(o8[2 * t + 1], __fmul_rn(f.y, pre[s]));
                                 }
                             }
                         }
                         uint4 o;
-                        o.x = f32x2_to_x2<DT>(acc[0], acc[1]);
-                        o.y = f32x2_to_x2<DT>(acc[2], acc[3]);
-                        o.z = f32x2_to_x2<DT>(acc[4], acc[5]);
-                        o.w = f32x2_to_x2<DT>(acc[6], acc[7]);
-                        __stcs(hr + vi + h * 128, o);
+                        o.x = f32x2_to_x2<DT>(o8[0], o8[1]);
+                        o.y = f32x2_to_x2<DT>(o8[2], o8[3]);
+                        o.z = f32x2_to_x2<DT>(o8[4], o8[5]);
+                        o.w = f32x2_to_x2<DT>(o8[6], o8[7]);
+                        __stcs(hr + vi + h * 32, o);
                     }
                 }
+                if (lane == 0) MHC_TRACE_EV(kTrRowDone, rlo, rhi);
             }
         }
     }
@@ -466,4 +463,5 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
         tc_fence_after();
         tmem_dealloc(tacc, Cfg::kTmemCols);
     }
+    if (threadIdx.x == 0) MHC_TRACE_EV(kTrKernelEnd, 5, 0);
 }

@@ -34,10 +34,14 @@ def pytest_sessionfinish(session, exitstatus):
     parity tests collected (hIn max ulp and exact-match rate, hPost/hRes max error)
     as JSON lines."""
     path = os.environ.get("MHC_PARITY_REPORT")
-    mod = sys.modules.get("tests.test_parity_gpu") or sys.modules.get("test_parity_gpu")
-    if not path or mod is None or not getattr(mod, "PARITY_STATS", None):
+    if not path:
         return
+    # the parity module is imported twice (by pytest as a test file, and by the other
+    # GPU test files as tests.test_parity_gpu): gather the statistics of both copies
+    stats = []
+    for name in ("test_parity_gpu", "tests.test_parity_gpu"):
+        stats += getattr(sys.modules.get(name), "PARITY_STATS", [])
     import json
     with open(path, "w") as f:
-        for st in mod.PARITY_STATS:
+        for st in stats:
             f.write(json.dumps(st) + "\n")

@@ -115,3 +115,18 @@ def test_library_reads_no_environment():
     csrc = ROOT / "mhcpre_review_b200" / "csrc"
     for f in list(csrc.glob("*.cu")) + list(csrc.glob("*.cuh")) + list(csrc.glob("*.cpp")) + list(csrc.glob("*.h")):
         assert "getenv" not in f.read_text(), f.name
+
+
+def test_trace_build_exports_trace_read():
+    """The trace build (-DMHC_TRACE) compiles and adds mhcPreTraceRead, declared in
+    include/mhc_pre_trace.h; the default library does not export it."""
+    from mhcpre_review_b200 import build
+
+    path = build.build(trace=True)
+    L = ctypes.CDLL(str(path))
+    text = (ROOT / "include" / "mhc_pre_trace.h").read_text()
+    for sym in re.findall(r"MHC_API\s+[\w\s\*]+?\b(mhcPre\w+)\s*\(", text):
+        assert hasattr(L, sym), sym
+    assert not hasattr(mp.lib(), "mhcPreTraceRead")
+    for s in declared_symbols():
+        assert hasattr(L, s), s
