@@ -310,7 +310,20 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
                 float ss = 0.0f;
                 for (int i = 0; i < nChunks; ++i, ++g) {
                     const int s = g % S;
-                    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>(g / S) & 1u, abortFlag))) {
+                    const uint32_t parity = static_cast<uint32_t>(g / S) & 1u;
+                    if (havePrev && prevLast &&
+                        !__all_sync(0xffffffffu, mbar_try_wait(smem_u32(&full[s]), parity))) {
+                        // A finished item's record is still pending (records are written
+                        // one segment late).  The next stage is not loaded yet: write the
+                        // record now, because the producer may be waiting for hIn warps
+                        // that wait for this very record.
+                        if (!retire_prev()) {
+                            ok = false;
+                            break;
+                        }
+                        havePrev = false;
+                    }
+                    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], parity, abortFlag))) {
                         ok = false;
                         break;
                     }

@@ -255,8 +255,11 @@ def parity_check(got, x_bits, phi, alpha, bias, gamma, n: int, D: int, dtype: st
     convention, cloud_runner/runner.cpp:287).  hIn: within 1 ulp of the x dtype; an
     element may differ by more only where the stream sum cancels, i.e. |got - ref| <=
     1 ulp + 1e-5 * sum_s |hPre_s x_s| (hPre carries the GEMM's ~1e-6 relative error
-    into hIn), and more than 99% of elements must match exactly.  Beyond K = 32768 the
-    budget grows with K, because fp32 sums over K (the oracle's sequential one
+    into hIn), or where got is at least as close as the oracle to the float64 value
+    sum_s hPre64_s x_s (within 1 ulp more): both are fp32 approximations, and where the
+    oracle's own sequential fp32 sum over K is the less accurate one, the difference
+    is the oracle's.  More than 99% of elements must match exactly.  Beyond K = 32768
+    the budget grows with K, because fp32 sums over K (the oracle's sequential one
     included) lose accuracy in proportion, and the exact-match floor is not applied
     (both sides are then fp32 approximations of the same float64 value)."""
     budget = HIN_BUDGET * max(1.0, n * D / 32768)
@@ -275,6 +278,7 @@ def parity_check(got, x_bits, phi, alpha, bias, gamma, n: int, D: int, dtype: st
     stats["hIn_exact"] = float((d == 0).mean())
     stats["hIn_max_ulp"] = int(d.max())
     stats["hIn_over_1ulp"] = int((d > 1).sum())
+    stats["hIn_closer_than_oracle"] = 0
     if (d > 1).any():
         bad_rows = np.nonzero((d > 1).any(axis=1))[0]
         xs = x_bits[bad_rows]
@@ -285,8 +289,11 @@ def parity_check(got, x_bits, phi, alpha, bias, gamma, n: int, D: int, dtype: st
         rf = to_float(r_in[bad_rows], dtype).astype(np.float64)
         ulp = ulp_size(r_in[bad_rows], dtype)
         ok = np.abs(gf - rf) <= ulp + budget * mag
+        h64 = np.einsum("rs,rsd->rd", pre64, xf)
+        closer = np.abs(gf - h64) <= np.abs(rf - h64) + ulp
         over = d[bad_rows] > 1
-        assert ok[over].all(), f"{label} hIn differs beyond 1 ulp without cancellation"
+        stats["hIn_closer_than_oracle"] = int((over & ~ok & closer).sum())
+        assert (ok | closer)[over].all(), f"{label} hIn differs beyond 1 ulp without cancellation"
     if n * D <= 32768:
         assert stats["hIn_exact"] > HIN_EXACT_MIN, f"{label} hIn exact-match rate {stats['hIn_exact']}"
     return stats

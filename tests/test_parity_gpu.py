@@ -6,8 +6,10 @@ Tolerances (stated by the operator's contract):
                cloud_runner/runner.cpp:287)
   hIn          within 1 ulp of the x dtype; an element may differ by more only where
                the stream sum cancels, i.e. |got - ref| <= 1 ulp + 1e-5 * sum_s |hPre_s x_s|
-               (hPre carries the GEMM's ~1e-6 relative error into hIn); the exact-match
-               rate must exceed 99%.  Beyond K = 32768 the budget grows with K, because
+               (hPre carries the GEMM's ~1e-6 relative error into hIn), or where the
+               GPU is at least as close as the oracle to the float64 value (within 1
+               ulp more; the oracle's sequential fp32 sum is then the less accurate
+               side); the exact-match rate must exceed 99%.  Beyond K = 32768 the budget grows with K, because
                fp32 sums over K (the oracle's sequential one included) lose accuracy in
                proportion; there, instead of the exact-match rate against the oracle,
                the GPU must be at least as close to a float64 restatement as the oracle
