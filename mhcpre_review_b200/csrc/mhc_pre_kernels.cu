@@ -974,26 +974,15 @@ static int launch_onepass_t(const Plan& plan, const CUtensorMap& xMap, const CUt
     static std::atomic<int> setBytes[kMaxDevices];
     cudaError_t e = ensure_smem(kern, setBytes, plan.smemBytes);
     if (e != cudaSuccess) return e;
-    int dev = 0, sms = 0, occ = 0;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, onepass_threads<EW>(), plan.smemBytes)) !=
-        cudaSuccess)
-        return e;
-    // every CTA must be resident (the hIn warps wait for other CTAs' items): one
-    // cooperative launch of at most the co-resident CTAs (results do not depend on G)
-    const int grid = std::min(plan.gemmGrid, std::max(1, std::min(occ, plan.opCtasPerSm)) * sms);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-    cfg.blockDim = dim3(onepass_threads<EW>(), 1, 1);
-    cfg.dynamicSmemBytes = plan.smemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, xMap, phiMap, op);
+    // The hIn warps wait for other CTAs' items, so every CTA must be resident: the
+    // grid is the CTAs per SM that the plan sized shared memory, registers and TMEM
+    // for (two or three) times the SMs.  It is an ordinary launch: the runtime's
+    // occupancy calculator reports one CTA per SM for kernels of this kind (the
+    // split-K GEMM included, which runs four), so a cooperative launch would be
+    // refused.  Should a CTA not be resident, the waits give up (bounded) and the
+    // call reports MHC_STATUS_DEVICE_TIMEOUT.
+    kern<<<plan.gemmGrid, onepass_threads<EW>(), plan.smemBytes, stream>>>(xMap, phiMap, op);
+    return cudaGetLastError();
 }
 
 static int launch_onepass(const Problem& p, const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiMap,

@@ -373,6 +373,8 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
                 const int slot = tile % p.RT;
                 const uint32_t rlo = static_cast<uint32_t>(static_cast<uint64_t>(r) & 0xffffffffu);
                 const uint32_t rhi = static_cast<uint32_t>(static_cast<uint64_t>(r) >> 32);
+                (void)rlo;  // trace arguments (used in the MHC_TRACE build only)
+                (void)rhi;
                 bool ok = true;
                 if (lane == 0) {
                     MHC_TRACE_EV(kTrRowWait, rlo, rhi);
