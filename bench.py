@@ -15,9 +15,12 @@ step time is the sum of the steps' own events.
 
 The JSON line also carries:
   roofline      the main kernel's algorithmic bytes per launch / its average launch
-                time (CUDA events recorded around that kernel inside the timed loop),
-                against the measured HBM copy bandwidth in MEASURED_PEAKS.json;
-                traffic = DRAM bytes per launch from the committed ncu summary.
+                time (CUDA events recorded around that kernel in a second loop of the
+                same steps right after the timed one, inside the same clock-sampled
+                region: events between kernels would stop the programmatic dependent
+                launches the timed loop uses), against the measured HBM copy
+                bandwidth in MEASURED_PEAKS.json; traffic = DRAM bytes per launch from
+                the committed ncu summary.
   cpu_baseline  the CPU oracle (a port of the reference's formula) timed on this
                 box's host cores on a bounded sample (rank 0, N=1).
   e2e           the same metric through the public API with host buffers: per step,
@@ -548,16 +551,31 @@ def other_configs(args, peak):
         for e in ev[2] + ev[3]:
             e.record()
         torch.cuda.synchronize()
+        if flush:
+            # each step alone between events, after its flush
+            for i in range(steps):
+                flush_buf.fill_(i & 0xFF)
+                ev[0][i].record()
+                ex(x, inp["alpha"], inp["bias"], out=out)
+                ev[1][i].record()
+            torch.cuda.synchronize()
+            ms = sum(b.elapsed_time(e) for b, e in zip(ev[0], ev[1])) / steps
+        else:
+            # back to back, as the headline loop
+            ev[0][0].record()
+            for i in range(steps):
+                ex(x, inp["alpha"], inp["bias"], out=out)
+            ev[1][0].record()
+            torch.cuda.synchronize()
+            ms = ev[0][0].elapsed_time(ev[1][0]) / steps
+        # the main kernel's launch times (a loop of its own: see main())
         for i in range(steps):
             if flush:
                 flush_buf.fill_(i & 0xFF)
-            ev[0][i].record()
             ex.run_profiled(x, inp["alpha"], inp["bias"], out, ev[2][i], ev[3][i])
-            ev[1][i].record()
         torch.cuda.synchronize()
         if mp.device_status() != 0:
             raise RuntimeError(f"device status after {name}")
-        ms = sum(b.elapsed_time(e) for b, e in zip(ev[0], ev[1])) / steps
         kms = sum(b.elapsed_time(e) for b, e in zip(ev[2], ev[3])) / steps
         plan = ex.plan
         kernel, kbytes = main_kernel(cfg, plan)
@@ -657,10 +675,21 @@ def main():
             if flush:
                 flush_buf.fill_(i & 0xFF)
                 op_b[i].record()
-            ex.run_profiled(x, inp["alpha"], inp["bias"], out, ev_b[i], ev_e[i])
+            ex(x, inp["alpha"], inp["bias"], out=out)
             if flush:
                 op_e[i].record()
         t_end.record()
+        torch.cuda.synchronize()
+        # The main kernel's launch times, for the roofline: the same steps again with
+        # CUDA events recorded on the launching stream around that kernel.  This is a
+        # loop of its own because an event between two kernels stops the second from
+        # launching early as a programmatic dependent of the first: the headline loop
+        # above has no events between its kernels (at 8192 rows per GPU, events
+        # around every launch cost about 9 us per step).
+        for i in range(args.steps):
+            if flush:
+                flush_buf.fill_(i & 0xFF)
+            ex.run_profiled(x, inp["alpha"], inp["bias"], out, ev_b[i], ev_e[i])
         torch.cuda.synchronize()
         if pg:
             dist.barrier()

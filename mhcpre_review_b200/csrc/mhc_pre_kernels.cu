@@ -247,6 +247,11 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_min_ctas<N>())
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // This grid is launched as a programmatic dependent of the kernel before it in the
+    // stream: the launch and the set-up above overlap that kernel's tail, and every
+    // thread waits here, before its first read of global memory, for that kernel to
+    // complete (its writes, x or the prepared weights among them, are then visible).
+    grid_dependency_wait();
     // the epilogue grid may start launching now; it waits for this grid in-kernel
     grid_launch_dependents();
     if (threadIdx.x == 0) MHC_TRACE_EV(kTrKernelBegin, 0, 0);
@@ -485,6 +490,9 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
     const int64_t r = p.M - 1 - blockIdx.x;
     const int tid = threadIdx.x;
     grid_dependency_wait();
+    // a following split-K GEMM may start launching (it waits for this grid before it
+    // reads or writes global memory)
+    grid_launch_dependents();
     if (tid == 0) MHC_TRACE_EV(kTrEpiRowBegin, static_cast<uint64_t>(r) & 0xffffffffu, static_cast<uint64_t>(r) >> 32);
     // sum over splits in split order, staged kEpiSplitBlock splits at a time
     float acc = 0.0f;
@@ -619,8 +627,18 @@ static int launch_gemm(const Plan& plan, const CUtensorMap& xMap, const CUtensor
     static std::atomic<int> setBytes[kMaxDevices];
     cudaError_t e = ensure_smem(kern, setBytes, plan.smemBytes);
     if (e != cudaSuccess) return e;
-    kern<<<plan.gemmGrid, kGemmThreads, plan.smemBytes, stream>>>(xMap, phiMap, gp);
-    return cudaGetLastError();
+    // programmatic dependent launch: see the wait at the top of the kernel
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.gemmGrid), 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = plan.smemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, xMap, phiMap, gp);
 }
 
 template <int DT, int NS>
