@@ -72,7 +72,9 @@ typedef enum {
     MHC_STATUS_UNSUPPORTED_DEVICE = -10, /* current device is not sm_100 */
     MHC_STATUS_DEVICE_TIMEOUT = -11,     /* a kernel gave up a bounded wait (see mhcPreGetDeviceStatus) */
     MHC_STATUS_NOT_PREPARED = -12,       /* mhcPreRunPrepared on a workspace without prepared weights */
-    MHC_STATUS_TOO_LARGE = -13           /* problem exceeds a documented size limit */
+    MHC_STATUS_TOO_LARGE = -13,          /* problem exceeds a documented size limit */
+    MHC_STATUS_INTERNAL_CHECK = -14      /* debug build only: a kernel's bounds check failed
+                                            (see include/mhc_pre_debug.h) */
 } mhcStatus_t;
 
 /* Problem description: the shape/attribute part of the aclnn executor.

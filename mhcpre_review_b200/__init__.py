@@ -23,6 +23,8 @@ _PKG = Path(__file__).resolve().parent
 LIB_PATH = _PKG / "libmhcpre_b200.so"
 # the same library built with -DMHC_TRACE: stage stamps, mhcPreTraceRead
 TRACE_LIB_PATH = _PKG / "libmhcpre_b200_trace.so"
+# ... and with -DMHC_DEBUG: bounds checks in the kernels (include/mhc_pre_debug.h)
+DEBUG_LIB_PATH = _PKG / "libmhcpre_b200_debug.so"
 
 F16 = 0
 BF16 = 1
@@ -31,6 +33,7 @@ STATUS_NAMES = {
     0: "SUCCESS", -1: "NULL_POINTER", -2: "BAD_SHAPE", -3: "BAD_STREAM_COUNT", -4: "BAD_HEAD_DIM",
     -5: "MIX_TOO_LARGE", -6: "BAD_DTYPE", -7: "MISALIGNED", -8: "WORKSPACE_TOO_SMALL", -9: "CUDA_ERROR",
     -10: "UNSUPPORTED_DEVICE", -11: "DEVICE_TIMEOUT", -12: "NOT_PREPARED", -13: "TOO_LARGE",
+    -14: "INTERNAL_CHECK",
 }
 
 EXPORTED_SYMBOLS = (
@@ -148,6 +151,11 @@ def lib():
         if hasattr(L, "mhcPreTraceRead"):
             L.mhcPreTraceRead.argtypes = [vp, sz, ctypes.POINTER(sz)]
             L.mhcPreTraceRead.restype = ctypes.c_int
+        if hasattr(L, "mhcPreDebugSetRecordCap"):
+            L.mhcPreDebugSetRecordCap.argtypes = [ctypes.c_int64]
+            L.mhcPreDebugSetRecordCap.restype = ctypes.c_int
+            L.mhcPreDebugLastCheckLine.argtypes = [ctypes.POINTER(ctypes.c_int32)]
+            L.mhcPreDebugLastCheckLine.restype = ctypes.c_int
         _libs[_lib_path] = L
     return L
 

@@ -13,6 +13,9 @@
 #ifdef MHC_TRACE
 #include "../../include/mhc_pre_trace.h"
 #endif
+#ifdef MHC_DEBUG
+#include "../../include/mhc_pre_debug.h"
+#endif
 
 namespace mhc {
 
@@ -455,6 +458,7 @@ const char* mhcPreStatusString(int status) {
         case MHC_STATUS_DEVICE_TIMEOUT: return "a kernel gave up a bounded wait";
         case MHC_STATUS_NOT_PREPARED: return "workspace holds no prepared weights";
         case MHC_STATUS_TOO_LARGE: return "problem exceeds a size limit";
+        case MHC_STATUS_INTERNAL_CHECK: return "a kernel's bounds check failed (debug build)";
         default: return "unknown status";
     }
 }
@@ -580,6 +584,22 @@ int mhcPreDiagWaitTimeout(uint32_t limitMicroseconds, int32_t* countersGaveUp, i
 MHC_API int mhcPreTraceRead(void* dst, size_t maxRecords, size_t* recorded) {
     if (recorded == nullptr) return MHC_STATUS_NULL_POINTER;
     return trace_read(dst, maxRecords, recorded) == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
+}
+#endif
+
+#ifdef MHC_DEBUG
+MHC_API int mhcPreDebugSetRecordCap(int64_t maxFloats) {
+    if (maxFloats < 0) return MHC_STATUS_BAD_SHAPE;
+    debug_set_record_cap(maxFloats);
+    return MHC_STATUS_SUCCESS;
+}
+
+MHC_API int mhcPreDebugLastCheckLine(int32_t* line) {
+    if (line == nullptr) return MHC_STATUS_NULL_POINTER;
+    int v = 0;
+    if (debug_last_check_line(&v) != 0) return MHC_STATUS_CUDA_ERROR;
+    *line = v;
+    return MHC_STATUS_SUCCESS;
 }
 #endif
 

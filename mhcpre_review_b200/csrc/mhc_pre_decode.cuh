@@ -50,6 +50,7 @@ struct DecodeParams {
     float* hPost;
     float* hRes;
     float* part;                     // [G][M][W]
+    int64_t partFloats;              // floats of part (bounds checks of the debug build)
     unsigned long long* barrier;     // WorkspaceHeader::gridBarrier
     const WorkspaceHeader* hdr;
     uint32_t signature;              // of the description (checked against the prepared weights)
@@ -230,7 +231,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) mhc_pre_decode_kernel(const
         float* rec = p.part + static_cast<int64_t>(g) * M * p.W;
         for (int i = tid; i < M * COLS; i += kDecodeThreads) {
             const int m = i / COLS, j = i - (i / COLS) * COLS;
-            rec[m * p.W + j] = j < MIX ? __fmul_rn(sacc[i], unscale) : sacc[i];
+            if (MHC_CHECK((static_cast<int64_t>(g) * M + m) * p.W + j < p.partFloats))
+                rec[m * p.W + j] = j < MIX ? __fmul_rn(sacc[i], unscale) : sacc[i];
         }
     }
 
@@ -274,8 +276,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) mhc_pre_decode_kernel(const
 #pragma unroll
                 for (int i = 0; i < 5; ++i) {
                     const int r = r0 + lane + 32 * i;
-                    vals[q][i] = (q < nc && r < G)
-                                     ? __ldcg(p.part + (static_cast<int64_t>(r) * M + m) * p.W + cols[q]) : 0.0f;
+                    const int64_t at = (static_cast<int64_t>(r) * M + m) * p.W + cols[q];
+                    vals[q][i] = (q < nc && r < G && MHC_CHECK(at < p.partFloats)) ? __ldcg(p.part + at) : 0.0f;
                 }
 #pragma unroll
             for (int q = 0; q <= NS; ++q)

@@ -112,6 +112,8 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
                void* workspace, cudaStream_t stream, cudaEvent_t evBegin = nullptr, cudaEvent_t evEnd = nullptr);
 int read_and_clear_device_status(int32_t* status);
 int trace_read(void* dst, size_t maxRecords, size_t* recorded);  // trace build only (MHC_TRACE)
+void debug_set_record_cap(int64_t floats);                        // debug build only (MHC_DEBUG)
+int debug_last_check_line(int* line);                             // debug build only (MHC_DEBUG)
 int launch_post(const Problem& p, const void* x, const void* y, const float* hPost, const float* hRes, void* xNext,
                 cudaStream_t stream);
 size_t decode_smem(const Problem& p);  // dynamic shared memory of the decode kernel

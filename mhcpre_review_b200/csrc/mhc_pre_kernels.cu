@@ -30,6 +30,23 @@ __device__ int g_device_status = 0;
 
 __device__ __forceinline__ void set_device_status(int code) { atomicCAS(&g_device_status, 0, code); }
 
+// Debug build (compile flag MHC_DEBUG; libmhcpre_b200_debug.so): MHC_CHECK(cond) guards
+// an access -- the caller performs it only when the check passes; a failed check
+// skips it, sets the device status word to MHC_STATUS_INTERNAL_CHECK and records the
+// source line (mhcPreDebugLastCheckLine).  In the default build it is the constant
+// true and costs nothing.
+#ifdef MHC_DEBUG
+__device__ int g_debug_line = 0;
+__device__ __noinline__ bool debug_check_failed(int line) {
+    set_device_status(MHC_STATUS_INTERNAL_CHECK);
+    atomicCAS(&g_debug_line, 0, line);
+    return false;
+}
+#define MHC_CHECK(cond) ((cond) ? true : ::mhc::debug_check_failed(__LINE__))
+#else
+#define MHC_CHECK(cond) true
+#endif
+
 // ---------------------------------------------------------------------------
 // 16-bit helpers
 // ---------------------------------------------------------------------------
@@ -131,6 +148,7 @@ struct GemmParams {
     int stages;
     uint32_t signature;  // of the description: the workspace must hold weights prepared for it
     float* partials;
+    int64_t partFloats;  // floats of the records buffer (bounds checks of the debug build)
     const WorkspaceHeader* hdr;
 };
 
@@ -409,8 +427,9 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_min_ctas<N>())
                 segBase += (nChunks + kSegChunks - 1) / kSegChunks;
                 if (!ok) break;
                 const int64_t grow = static_cast<int64_t>(tile) * kRowsPerTile + row;
-                if (grow < p.M) {
-                    float* out = p.partials + (static_cast<int64_t>(split) * p.M + grow) * p.W;
+                const int64_t recAt = (static_cast<int64_t>(split) * p.M + grow) * p.W;
+                if (grow < p.M && MHC_CHECK(split < p.splits && recAt + MIX < p.partFloats)) {
+                    float* out = p.partials + recAt;
 #pragma unroll
                     for (int j0 = 0; j0 < MIX; j0 += 4) {
                         float4 a;
@@ -452,6 +471,7 @@ struct EpiParams {
     float normEps;
     float hcEps;
     const float* partials;
+    int64_t partFloats;  // floats of the records buffer (bounds checks of the debug build)
     const uint16_t* x;
     const float* alpha;
     const float* bias;
@@ -503,7 +523,8 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
         for (int i = tid; i < vals; i += kEpiThreads) {
             const int sp = i / cols;
             const int j = i - sp * cols;
-            sPart[i] = __ldcg(p.partials + (static_cast<int64_t>(sp0 + sp) * p.M + r) * p.W + j);
+            const int64_t at = (static_cast<int64_t>(sp0 + sp) * p.M + r) * p.W + j;
+            sPart[i] = MHC_CHECK(at < p.partFloats && i < kEpiSplitBlock * cols) ? __ldcg(p.partials + at) : 0.0f;
         }
         __syncthreads();
         if (tid < cols)
@@ -581,6 +602,26 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
+#ifdef MHC_DEBUG
+// Debug build: a cap on the records-buffer size the kernels are told (0: none), so
+// a test can make their bounds checks fail on purpose without any access outside a
+// buffer (a failed check skips the access).
+static std::atomic<int64_t> g_debug_record_cap{0};
+void debug_set_record_cap(int64_t floats) { g_debug_record_cap.store(floats); }
+int debug_last_check_line(int* line) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(line, g_debug_line, sizeof(int));
+    const int zero = 0;
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_debug_line, &zero, sizeof(int));
+    return e;
+}
+static int64_t debug_record_limit(int64_t floats) {
+    const int64_t cap = g_debug_record_cap.load();
+    return cap > 0 && cap < floats ? cap : floats;
+}
+#else
+static int64_t debug_record_limit(int64_t floats) { return floats; }
+#endif
 int launch_prepare(const Problem& p, const Plan& plan, const float* phi, const float* gamma, void* workspace,
                    cudaStream_t stream) {
     auto* hdr = reinterpret_cast<WorkspaceHeader*>(workspace);
@@ -764,6 +805,7 @@ static int launch_decode(const Problem& p, const Plan& plan, const void* x, cons
     dp.hPost = hPost;
     dp.hRes = hRes;
     dp.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.partOffset);
+    dp.partFloats = debug_record_limit(static_cast<int64_t>(plan.partBytes / 4));
     dp.barrier = &hdr->gridBarrier;
     dp.hdr = hdr;
     dp.signature = p.signature;
@@ -858,6 +900,7 @@ static int launch_small(const Problem& p, const Plan& plan, const CUtensorMap& x
     sp.hPost = hPost;
     sp.hRes = hRes;
     sp.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.partOffset);
+    sp.partFloats = debug_record_limit(static_cast<int64_t>(plan.partBytes / 4));
     sp.barrier = &hdr->gridBarrier;
     sp.hdr = hdr;
     if (evBegin != nullptr && cudaEventRecord(evBegin, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
@@ -1031,6 +1074,7 @@ static int launch_onepass(const Problem& p, const Plan& plan, const CUtensorMap&
     op.hPost = hPost;
     op.hRes = hRes;
     op.rec = reinterpret_cast<float*>(ws + plan.partOffset);
+    op.recFloats = debug_record_limit(static_cast<int64_t>(plan.partBytes / 4));
     op.cnt = reinterpret_cast<unsigned*>(ws + plan.cntOffset);
     op.hdr = reinterpret_cast<const WorkspaceHeader*>(workspace);
     if (evBegin != nullptr && cudaEventRecord(evBegin, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
@@ -1072,6 +1116,7 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
     gp.stages = plan.stages;
     gp.signature = p.signature;
     gp.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.partOffset);
+    gp.partFloats = debug_record_limit(static_cast<int64_t>(plan.partBytes / 4));
     gp.hdr = reinterpret_cast<const WorkspaceHeader*>(workspace);
     int rc;
     const bool bf = p.dtype == MHC_DTYPE_BF16;
@@ -1097,6 +1142,7 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
     ep.normEps = p.normEps;
     ep.hcEps = p.hcEps;
     ep.partials = gp.partials;
+    ep.partFloats = gp.partFloats;
     ep.x = static_cast<const uint16_t*>(x);
     ep.alpha = alpha;
     ep.bias = bias;

@@ -55,6 +55,7 @@ struct OnePassParams {
     float* hPost;
     float* hRes;
     float* rec;      // [RT][128][splits][W]
+    int64_t recFloats;  // floats of rec (bounds checks of the debug build)
     unsigned* cnt;   // [RT] record arrivals (4 per item), [RT] rows consumed, [1] abort word
     const WorkspaceHeader* hdr;
 };
@@ -282,9 +283,9 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
                     if (!__shfl_sync(0xffffffffu, freed ? 1 : 0, 0)) return false;
                 }
                 const int64_t grow = static_cast<int64_t>(prevTile) * kRowsPerTile + row;
-                if (grow < p.M) {
-                    float* out =
-                        p.rec + ((static_cast<int64_t>(slot) * kRowsPerTile + row) * p.splits + prevSplit) * p.W;
+                const int64_t recAt = ((static_cast<int64_t>(slot) * kRowsPerTile + row) * p.splits + prevSplit) * p.W;
+                if (grow < p.M && MHC_CHECK(slot < p.RT && prevSplit < p.splits && recAt + MIX < p.recFloats)) {
+                    float* out = p.rec + recAt;
 #pragma unroll
                     for (int j0 = 0; j0 < MIX; j0 += 4) {
                         float4 a;
@@ -387,8 +388,9 @@ __global__ void __launch_bounds__(onepass_threads<EW>(), MINB)
                 }
                 // lane j sums record column j over the splits, in split order
                 float acc = 0.0f;
-                if (lane <= MIX) {
-                    const float* col = p.rec + (static_cast<int64_t>(slot) * kRowsPerTile + lrow) * p.splits * p.W + lane;
+                const int64_t rowAt = (static_cast<int64_t>(slot) * kRowsPerTile + lrow) * p.splits * p.W;
+                if (lane <= MIX && MHC_CHECK(rowAt + static_cast<int64_t>(p.splits) * p.W <= p.recFloats)) {
+                    const float* col = p.rec + rowAt + lane;
                     constexpr int kB = 28;  // loads in flight per lane
                     int sp = 0;
                     for (; sp + kB <= p.splits; sp += kB) {

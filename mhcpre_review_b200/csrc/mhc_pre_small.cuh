@@ -50,6 +50,7 @@ struct SmallParams {
     float* hPost;
     float* hRes;
     float* part;                  // [G][M][W]
+    int64_t partFloats;           // floats of part (bounds checks of the debug build)
     unsigned long long* barrier;  // WorkspaceHeader::gridBarrier
     const WorkspaceHeader* hdr;
 };
@@ -295,9 +296,10 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
                 if (lane == 0) fail();
             } else {
                 const int m = tw * kRowsPerTile + row;
-                if (m < M) {
+                const int64_t recAt = (static_cast<int64_t>(g) * M + m) * p.W;
+                if (m < M && MHC_CHECK(recAt + MIX < p.partFloats)) {
                     const float unscale = ldexpf(1.0f, -p.hdr->phiScaleExp);
-                    float* out = p.part + (static_cast<int64_t>(g) * M + m) * p.W;
+                    float* out = p.part + recAt;
 #pragma unroll
                     for (int j0 = 0; j0 < MIX; j0 += 4) {
                         float4 a;
@@ -363,8 +365,11 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
                 for (int i = 0; i < kRecBatch; ++i)
 #pragma unroll
                     for (int c = 0; c < CPL; ++c)
-                        v[i][c] = (r0 + i < re && lane + 32 * c < COLS) ? __ldcg(rp + (r0 + i) * recStride + 32 * c)
-                                                                        : 0.0f;
+                        v[i][c] = (r0 + i < re && lane + 32 * c < COLS &&
+                                   MHC_CHECK(static_cast<int64_t>(m) * p.W + lane + (r0 + i) * recStride + 32 * c <
+                                             p.partFloats))
+                                      ? __ldcg(rp + (r0 + i) * recStride + 32 * c)
+                                      : 0.0f;
 #pragma unroll
                 for (int i = 0; i < kRecBatch; ++i)
                     if (r0 + i < re)

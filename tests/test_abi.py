@@ -130,3 +130,17 @@ def test_trace_build_exports_trace_read():
     assert not hasattr(mp.lib(), "mhcPreTraceRead")
     for s in declared_symbols():
         assert hasattr(L, s), s
+
+
+def test_debug_build_exports_its_entry_points():
+    """The debug build (-DMHC_DEBUG) compiles and adds the entry points of
+    include/mhc_pre_debug.h; the default library does not export them."""
+    from mhcpre_review_b200 import build
+
+    path = build.build(debug=True)
+    L = ctypes.CDLL(str(path))
+    text = (ROOT / "include" / "mhc_pre_debug.h").read_text()
+    syms = re.findall(r"MHC_API\s+[\w\s\*]+?\b(mhcPre\w+)\s*\(", text)
+    assert len(syms) == 2
+    for sym in syms:
+        assert hasattr(L, sym) and not hasattr(mp.lib(), sym), sym
