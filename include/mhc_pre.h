@@ -203,7 +203,9 @@ typedef struct {
                               1: first read evict_last, re-read evict_first, the default;
                               2: re-read evict_first only) */
     int32_t ringTiles;     /* one-pass path: tile slots of the partial-record ring */
-    int32_t reserved[7];   /* must be 0 */
+    int32_t pairedGemm;    /* split-K path at n = 8: 0 the library's choice, 1 one-CTA GEMM,
+                              2 GEMM on CTA pairs (one M = 256 tcgen05 MMA per pair) */
+    int32_t reserved[6];   /* must be 0 */
 } mhcPrePlanOptions_t;
 
 /* mhcPreGetWorkspaceSize / mhcPreQueryPlan / mhcPrePrepareWeights /

@@ -70,7 +70,7 @@ constexpr int64_t kShardRows = 8192;  // from this M up, splits depend on K only
 constexpr int kMinSplitChunks = 6;    // smallest split below kShardRows rows
 
 int make_plan(const Problem& p, int smCount, const mhcPrePlanOptions_t* opt, Plan* plan) {
-    static const mhcPrePlanOptions_t kDefaults = {MHC_PRE_PATH_AUTO, 0, 0, 0, 0, 0, 0, 0, 0, {0, 0, 0, 0, 0, 0, 0}};
+    static const mhcPrePlanOptions_t kDefaults = {MHC_PRE_PATH_AUTO, 0, 0, 0, 0, 0, 0, 0, 0, 0, {0, 0, 0, 0, 0, 0}};
     const mhcPrePlanOptions_t& o = opt != nullptr ? *opt : kDefaults;
     const bool autoPath = o.path == MHC_PRE_PATH_AUTO;
     Plan pl{};
@@ -118,6 +118,17 @@ int make_plan(const Problem& p, int smCount, const mhcPrePlanOptions_t* opt, Pla
     pl.lead = 0;
     pl.gemmGrid = std::min(pl.tilesM * splits, smCount * ctasPerSm);
     pl.smemBytes = fixed + static_cast<size_t>(stages) * stageBytes;
+    // n = 8: the GEMM on CTA pairs when plan options ask for it (the same splits,
+    // so the same result bits): items are (256-row pair tile, split), one pair per
+    // SM's worth of CTA slots, four 26 KB stages per CTA.
+    pl.pairGemm = p.N == 160 && o.pairedGemm == 2;
+    if (pl.pairGemm) {
+        const int pairTiles = (pl.tilesM + 1) / 2;
+        pl.stages = std::max(2, std::min(o.gemmStages > 0 ? o.gemmStages : 4, 4));
+        pl.tmaBatch = o.tmaBatch > 0 ? std::min(o.tmaBatch, pl.stages) : std::min(4, pl.stages / 2);
+        pl.gemmGrid = 2 * std::min(pairTiles * splits, smCount);
+        pl.smemBytes = pair_smem_bytes(pl.stages);
+    }
     pl.phiOffset = sizeof(WorkspaceHeader);
     pl.phiBytes = static_cast<size_t>(p.N) * static_cast<size_t>(p.K) * 2;
     pl.partOffset = align_up(pl.phiOffset + pl.phiBytes, 256);
@@ -365,6 +376,7 @@ static int encode_2d(EncodeTiledFn enc, CUtensorMap* map, const void* base, int 
 static int options_ok(const mhcPrePlanOptions_t* opt) {
     if (opt == nullptr) return MHC_STATUS_SUCCESS;
     if (opt->path < MHC_PRE_PATH_AUTO || opt->path > 5) return MHC_STATUS_BAD_SHAPE;
+    if (opt->pairedGemm < 0 || opt->pairedGemm > 2) return MHC_STATUS_BAD_SHAPE;
     for (int r : opt->reserved)
         if (r != 0) return MHC_STATUS_BAD_SHAPE;
     return MHC_STATUS_SUCCESS;
@@ -412,8 +424,9 @@ static int run_prepared(const Problem& p, const Plan& plan, const void* x, const
     int rc = encode_2d(enc, &xMap, x, p.dtype, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M), kRowsPerTile);
     if (rc != 0) return rc;
     const void* phiPrep = static_cast<const uint8_t*>(workspace) + plan.phiOffset;
+    // the CTA-pair GEMM stages half of the weight rows in each CTA
     rc = encode_2d(enc, &phiMap, phiPrep, p.dtype, static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.N),
-                   static_cast<uint32_t>(p.N));
+                   static_cast<uint32_t>(plan.path == 0 && plan.pairGemm ? p.N / 2 : p.N));
     if (rc != 0) return rc;
     const int e =
         launch_run(p, plan, xMap, phiMap, x, alpha, bias, hIn, hPost, hRes, workspace, stream, evBegin, evEnd);

@@ -90,7 +90,16 @@ struct Plan {
     // path 5 (one pass): record ring slots and CTAs per SM
     int ringTiles;
     int opCtasPerSm;
+    // path 0 at n = 8: the GEMM runs on CTA pairs (one M = 256 MMA, cta_group::2)
+    bool pairGemm;
 };
+
+// Shared memory of the CTA-pair GEMM (n = 8): stages of a 128-row x tile and half of
+// the 160 weight rows of one 64-wide chunk.
+constexpr size_t kPairStageBytesHost = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + 80 * kChunk * 2;
+constexpr size_t pair_smem_bytes(int stages) {
+    return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * kPairStageBytesHost + 512 /*barriers*/;
+}
 
 // One-pass kernel (path 5) layout constants, shared by the plan and the launcher.
 constexpr int kOnePassItemChunks = 4;  // default 64-wide chunks per work item

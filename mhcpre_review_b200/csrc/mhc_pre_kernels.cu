@@ -594,6 +594,7 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
 
 #include "mhc_pre_fused.cuh"
 #include "mhc_pre_cluster.cuh"
+#include "mhc_pre_pair.cuh"
 #include "mhc_pre_decode.cuh"
 #include "mhc_pre_small.cuh"
 #include "mhc_pre_onepass.cuh"
@@ -680,6 +681,32 @@ static int launch_gemm(const Plan& plan, const CUtensorMap& xMap, const CUtensor
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, xMap, phiMap, gp);
+}
+
+template <int DT>
+static int launch_gemm_pair(const Plan& plan, const CUtensorMap& xMap, const CUtensorMap& phiHalfMap,
+                            const GemmParams& gp, cudaStream_t stream) {
+    auto kern = gemm_pair_kernel<DT>;
+    static std::atomic<int> setBytes[kMaxDevices];
+    cudaError_t e = ensure_smem(kern, setBytes, plan.smemBytes);
+    if (e != cudaSuccess) return e;
+    // clusters of two CTAs (the pair), launched as a programmatic dependent like the
+    // one-CTA GEMM.  Pairs never wait on other pairs: they need not all be resident.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.gemmGrid), 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = plan.smemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, xMap, phiHalfMap, gp);
 }
 
 template <int DT, int NS>
@@ -1126,8 +1153,14 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
                         : launch_gemm<MHC_DTYPE_F16, 48>(plan, xMap, phiMap, gp, stream); break;
         case 6: rc = bf ? launch_gemm<MHC_DTYPE_BF16, 96>(plan, xMap, phiMap, gp, stream)
                         : launch_gemm<MHC_DTYPE_F16, 96>(plan, xMap, phiMap, gp, stream); break;
-        default: rc = bf ? launch_gemm<MHC_DTYPE_BF16, 160>(plan, xMap, phiMap, gp, stream)
-                         : launch_gemm<MHC_DTYPE_F16, 160>(plan, xMap, phiMap, gp, stream); break;
+        default:
+            if (plan.pairGemm)
+                rc = bf ? launch_gemm_pair<MHC_DTYPE_BF16>(plan, xMap, phiMap, gp, stream)
+                        : launch_gemm_pair<MHC_DTYPE_F16>(plan, xMap, phiMap, gp, stream);
+            else
+                rc = bf ? launch_gemm<MHC_DTYPE_BF16, 160>(plan, xMap, phiMap, gp, stream)
+                        : launch_gemm<MHC_DTYPE_F16, 160>(plan, xMap, phiMap, gp, stream);
+            break;
     }
     if (rc != 0) return rc;
     if (evEnd != nullptr && cudaEventRecord(evEnd, stream) != cudaSuccess) return cudaErrorInvalidResourceHandle;
