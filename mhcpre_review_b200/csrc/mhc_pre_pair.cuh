@@ -156,6 +156,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     tc_fence_after();
     grid_dependency_wait();   // as in the one-CTA GEMM: the kernel before this one is complete
     grid_launch_dependents();
+    if (threadIdx.x == 0) MHC_TRACE_EV(kTrKernelBegin, 0, rank);
     const uint32_t tacc = *tmemSlot;
     const bool prepared = p.hdr->magic == kPreparedMagic && p.hdr->signature == p.signature;
     if (!prepared && threadIdx.x == 0) set_device_status(MHC_STATUS_NOT_PREPARED);
@@ -180,6 +181,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
                     int ptile, split, cBegin, nChunks;
                     item_range(w, ptile, split, cBegin, nChunks);
                     const int rowBase = ptile * 2 * kRowsPerTile + static_cast<int>(rank) * kRowsPerTile;
+                    MHC_TRACE_EV(kTrGemmItemBegin, ptile, split);
                     for (int i0 = 0; i0 < nChunks && !*abortFlag; i0 += batch) {
                         const int nb = min(batch, nChunks - i0);
                         bool okb = true;
@@ -328,6 +330,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
                     }
                     out[MIX] = ss;
                 }
+                if (warp == 2 && lane == 0) MHC_TRACE_EV(kTrGemmRecord, ptile, split);
             }
             if (!ok && lane == 0) fail();
         }
@@ -344,4 +347,5 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         tc_fence_after();
         tmem_dealloc_pair(tacc, kPairTmemCols);
     }
+    if (threadIdx.x == 0) MHC_TRACE_EV(kTrKernelEnd, 0, rank);
 }
