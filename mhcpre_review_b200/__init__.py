@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "mhcPreRunPreparedProfiled", "mhcPreQueryPlan", "mhcPreGetDeviceStatus", "mhcPreStatusString",
     "mhcPreAbiVersion", "mhcPreRunNoAlloc", "mhcPreDiagWaitTimeout", "mhcPostRun",
     "mhcPreGetWorkspaceSizeEx", "mhcPreQueryPlanEx", "mhcPrePrepareWeightsEx", "mhcPreRunPreparedEx",
+    "mhcPostPreRun",
 )
 
 PATH_AUTO = -1
@@ -136,6 +137,7 @@ def lib():
         L.mhcPreQueryPlan.argtypes = [dp, ctypes.POINTER(MhcPrePlan)]
         L.mhcPreRunNoAlloc.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
         L.mhcPostRun.argtypes = [dp, vp, vp, vp, vp, vp, vp]
+        L.mhcPostPreRun.argtypes = [dp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, sz, vp]
         L.mhcPreGetDeviceStatus.argtypes = [ctypes.POINTER(ctypes.c_int32)]
         op = ctypes.POINTER(MhcPrePlanOptions)
         L.mhcPreGetWorkspaceSizeEx.argtypes = [dp, op, ctypes.POINTER(sz)]
@@ -366,6 +368,29 @@ class MhcPre:
                                              ctypes.c_void_p(ev_begin.cuda_event),
                                              ctypes.c_void_p(ev_end.cuda_event)), "RunPreparedProfiled")
         return hIn, hPost, hRes
+
+    def post_and_run(self, x, y, hPost, hRes, alpha, bias, x_next=None, out=None, stream=None):
+        """The previous layer's post step fused with this executor's MhcPre
+        (mhcPostPreRun): x_next = sum_t hRes[..., s, t] * x[..., t, :] + hPost[..., s] * y,
+        then MhcPre on x_next with the prepared weights.  x: [B, S, n, D] (the streams
+        the previous layer read), y: [B, S, D] its output, hPost/hRes its fp32
+        coefficients.  Returns (x_next, (hIn, hPost, hRes)); x_next may be x."""
+        torch = _torch()
+        d = self.desc
+        x_dtype = torch.bfloat16 if d.dtype == BF16 else torch.float16
+        _require(x, "x", self.device, x_dtype, (d.batch, d.seq, d.streams, d.headDim))
+        _require(y, "y", self.device, x_dtype, (d.batch, d.seq, d.headDim))
+        _require(hPost, "hPost", self.device, torch.float32, (d.batch, d.seq, d.streams))
+        _require(hRes, "hRes", self.device, torch.float32, (d.batch, d.seq, d.streams, d.streams))
+        if x_next is None:
+            x_next = torch.empty_like(x)
+        _check_run(d, self.device, x_next, alpha, bias, out)
+        hIn, hPostN, hResN = out if out is not None else self.outputs(x_dtype)
+        with torch.cuda.device(self.device):
+            _check(lib().mhcPostPreRun(ctypes.byref(d), _ptr(x), _ptr(y), _ptr(hPost), _ptr(hRes), _ptr(x_next),
+                                       _ptr(alpha), _ptr(bias), _ptr(hIn), _ptr(hPostN), _ptr(hResN),
+                                       _ptr(self.workspace), self.ws_bytes, _stream_ptr(stream)), "PostPreRun")
+        return x_next, (hIn, hPostN, hResN)
 
     def __call__(self, x, alpha, bias, out=None, stream=None):
         torch = _torch()

@@ -26,7 +26,8 @@ TRACE_LIB = PKG / "libmhcpre_b200_trace.so"
 DEBUG_LIB = PKG / "libmhcpre_b200_debug.so"
 SOURCES = ["mhc_pre_kernels.cu", "mhc_pre_api.cpp", "mhc_pre_noalloc.cu"]
 HEADERS = ["ptx.cuh", "mhc_pre_internal.h", "mhc_pre_fused.cuh", "mhc_pre_decode.cuh", "mhc_pre_cluster.cuh",
-           "mhc_pre_small.cuh", "mhc_pre_onepass.cuh", "mhc_pre_pair.cuh", "mhc_post.cuh", "trace.cuh"]
+           "mhc_pre_small.cuh", "mhc_pre_onepass.cuh", "mhc_pre_pair.cuh", "mhc_post.cuh", "mhc_post_pre.cuh",
+           "trace.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -576,6 +576,45 @@ int mhcPostRun(const mhcPreDesc_t* desc, const void* x, const void* y, const flo
     return e == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
 }
 
+int mhcPostPreRun(const mhcPreDesc_t* desc, const void* x, const void* y, const float* hPost, const float* hRes,
+                  void* xNext, const float* alpha, const float* bias, void* hIn, float* hPostNext, float* hResNext,
+                  void* workspace, size_t workspaceBytes, void* stream) {
+    Problem p;
+    Plan plan;
+    int rc = prepare_common(desc, nullptr, &p, &plan, workspaceBytes, workspace);
+    if (rc != 0) return rc;
+    if (x == nullptr || y == nullptr || hPost == nullptr || hRes == nullptr || xNext == nullptr ||
+        alpha == nullptr || bias == nullptr || hIn == nullptr || hPostNext == nullptr || hResNext == nullptr)
+        return MHC_STATUS_NULL_POINTER;
+    if (!aligned16(x) || !aligned16(y) || !aligned16(xNext) || !aligned4(hPost) || !aligned4(hRes))
+        return MHC_STATUS_MISALIGNED;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (!post_pre_applies(p, plan)) {
+        // the two steps one after the other
+        if (launch_post(p, x, y, hPost, hRes, xNext, st) != 0) return MHC_STATUS_CUDA_ERROR;
+        return run_prepared(p, plan, xNext, alpha, bias, hIn, hPostNext, hResNext, workspace, st);
+    }
+    if (!aligned16(hIn) || !aligned4(hPostNext) || !aligned4(hResNext) || !aligned4(alpha) || !aligned4(bias))
+        return MHC_STATUS_MISALIGNED;
+    int sms = 0;
+    rc = device_sm_count(&sms);
+    if (rc != 0) return rc;
+    const PostPrePlan pp = make_post_pre_plan(p, plan, sms);
+    EncodeTiledFn enc = get_encode_fn();
+    if (enc == nullptr) return MHC_STATUS_CUDA_ERROR;
+    CUtensorMap xMap{}, yMap{}, xNextMap{}, phiMap{};
+    const uint64_t K = static_cast<uint64_t>(p.K), M = static_cast<uint64_t>(p.M), D = static_cast<uint64_t>(p.D);
+    if ((rc = encode_2d(enc, &xMap, x, p.dtype, K, M, kRowsPerTile)) != 0) return rc;
+    if ((rc = encode_2d(enc, &yMap, y, p.dtype, D, M, kRowsPerTile)) != 0) return rc;
+    if ((rc = encode_2d(enc, &xNextMap, xNext, p.dtype, K, M, kRowsPerTile)) != 0) return rc;
+    const void* phiPrep = static_cast<const uint8_t*>(workspace) + plan.phiOffset;
+    if ((rc = encode_2d(enc, &phiMap, phiPrep, p.dtype, K, static_cast<uint64_t>(p.N), static_cast<uint32_t>(p.N))) != 0)
+        return rc;
+    const int e = launch_post_pre(p, pp, plan, xMap, yMap, xNextMap, phiMap, hPost, hRes, xNext, alpha, bias, hIn,
+                                  hPostNext, hResNext, workspace, st);
+    return e == 0 ? MHC_STATUS_SUCCESS : MHC_STATUS_CUDA_ERROR;
+}
+
 int mhcPreDiagWaitTimeout(uint32_t limitMicroseconds, int32_t* countersGaveUp, int32_t* barriersGaveUp,
                           void* stream) {
     if (countersGaveUp == nullptr || barriersGaveUp == nullptr) return MHC_STATUS_NULL_POINTER;

@@ -94,6 +94,29 @@ struct Plan {
     bool pairGemm;
 };
 
+// The post step fused with the next MhcPre's contraction (n = 4, D % 64 == 0): a stage
+// holds the x tiles of the 4 streams and the y tile of one 64-wide d-chunk (16 KB
+// each) and the 4 weight chunks of N = 48 rows (6 KB each).
+constexpr size_t kPostPreStageBytesHost = 5 * static_cast<size_t>(kRowsPerTile) * kChunk * 2 + 4 * 48 * kChunk * 2;
+constexpr int kPostPreStages = 2;
+constexpr size_t post_pre_smem_bytes(int stages) {
+    return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * kPostPreStageBytesHost + 256 /*barriers*/ +
+           128 * 4 /*sums of squares*/;
+}
+struct PostPrePlan {
+    int tilesM, dChunks, splits, stages, grid;
+    size_t smemBytes;
+};
+// The fused path applies (n = 4, D % 64 == 0, and the default MhcPre plan is the
+// split-K path); its splits never exceed the split-K plan's, so the workspace of
+// mhcPreGetWorkspaceSize suffices.
+bool post_pre_applies(const Problem& p, const Plan& defaultPlan);
+PostPrePlan make_post_pre_plan(const Problem& p, const Plan& defaultPlan, int smCount);
+int launch_post_pre(const Problem& p, const PostPrePlan& pp, const Plan& plan, const CUtensorMap& xMap,
+                    const CUtensorMap& yMap, const CUtensorMap& xNextMap, const CUtensorMap& phiMap,
+                    const float* hPost, const float* hRes, const void* xNext, const float* alpha, const float* bias,
+                    void* hIn, float* hPostNext, float* hResNext, void* workspace, cudaStream_t stream);
+
 // Shared memory of the CTA-pair GEMM (n = 8): stages of a 128-row x tile and half of
 // the 160 weight rows of one 64-wide chunk.
 constexpr size_t kPairStageBytesHost = static_cast<size_t>(kRowsPerTile) * kChunk * 2 + 80 * kChunk * 2;

@@ -599,6 +599,7 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiPara
 #include "mhc_pre_small.cuh"
 #include "mhc_pre_onepass.cuh"
 #include "mhc_post.cuh"
+#include "mhc_post_pre.cuh"
 
 // ---------------------------------------------------------------------------
 // Launchers
@@ -1187,6 +1188,90 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
         case 6: return bf ? launch_epi<MHC_DTYPE_BF16, 6>(p, ep, stream) : launch_epi<MHC_DTYPE_F16, 6>(p, ep, stream);
         default: return bf ? launch_epi<MHC_DTYPE_BF16, 8>(p, ep, stream) : launch_epi<MHC_DTYPE_F16, 8>(p, ep, stream);
     }
+}
+
+// ---------------------------------------------------------------------------
+// The post step fused with the next MhcPre's contraction, then the split-K epilogue
+// ---------------------------------------------------------------------------
+bool post_pre_applies(const Problem& p, const Plan& defaultPlan) {
+    return p.n == kPostPreNS && p.D % kChunk == 0 && defaultPlan.path == 0;
+}
+
+PostPrePlan make_post_pre_plan(const Problem& p, const Plan& defaultPlan, int smCount) {
+    PostPrePlan pp{};
+    pp.tilesM = defaultPlan.tilesM;
+    pp.dChunks = static_cast<int>(p.D / kChunk);
+    // as many splits as the split-K plan (so the same workspace holds the records),
+    // at most one per d-chunk
+    pp.splits = std::max(1, std::min(defaultPlan.splits, pp.dChunks));
+    pp.stages = kPostPreStages;
+    pp.grid = std::min(pp.tilesM * pp.splits, smCount);  // one CTA per SM
+    pp.smemBytes = post_pre_smem_bytes(pp.stages);
+    return pp;
+}
+
+template <int DT>
+static int launch_post_pre_kernel(const PostPrePlan& pp, const CUtensorMap& xMap, const CUtensorMap& yMap,
+                                  const CUtensorMap& xNextMap, const CUtensorMap& phiMap, const PostPreParams& prm,
+                                  cudaStream_t stream) {
+    auto kern = post_pre_kernel<DT>;
+    static std::atomic<int> setBytes[kMaxDevices];
+    cudaError_t e = ensure_smem(kern, setBytes, pp.smemBytes);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(pp.grid), 1, 1);
+    cfg.blockDim = dim3(kPostPreThreads, 1, 1);
+    cfg.dynamicSmemBytes = pp.smemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, xMap, yMap, xNextMap, phiMap, prm);
+}
+
+int launch_post_pre(const Problem& p, const PostPrePlan& pp, const Plan& plan, const CUtensorMap& xMap,
+                    const CUtensorMap& yMap, const CUtensorMap& xNextMap, const CUtensorMap& phiMap,
+                    const float* hPost, const float* hRes, const void* xNext, const float* alpha, const float* bias,
+                    void* hIn, float* hPostNext, float* hResNext, void* workspace, cudaStream_t stream) {
+    PostPreParams prm;
+    prm.M = p.M;
+    prm.D = p.D;
+    prm.tilesM = pp.tilesM;
+    prm.dChunks = pp.dChunks;
+    prm.splits = pp.splits;
+    prm.stages = pp.stages;
+    prm.W = p.W;
+    prm.signature = p.signature;
+    prm.hPost = hPost;
+    prm.hRes = hRes;
+    prm.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.partOffset);
+    prm.partFloats = debug_record_limit(static_cast<int64_t>(plan.partBytes / 4));
+    prm.hdr = reinterpret_cast<const WorkspaceHeader*>(workspace);
+    const bool bf = p.dtype == MHC_DTYPE_BF16;
+    int rc = bf ? launch_post_pre_kernel<MHC_DTYPE_BF16>(pp, xMap, yMap, xNextMap, phiMap, prm, stream)
+                : launch_post_pre_kernel<MHC_DTYPE_F16>(pp, xMap, yMap, xNextMap, phiMap, prm, stream);
+    if (rc != 0) return rc;
+    EpiParams ep;
+    ep.M = p.M;
+    ep.D = p.D;
+    ep.K = p.K;
+    ep.mix = p.mix;
+    ep.W = p.W;
+    ep.splits = pp.splits;
+    ep.invK = 1.0f / static_cast<float>(p.K);
+    ep.normEps = p.normEps;
+    ep.hcEps = p.hcEps;
+    ep.partials = prm.partials;
+    ep.partFloats = prm.partFloats;
+    ep.x = static_cast<const uint16_t*>(xNext);
+    ep.alpha = alpha;
+    ep.bias = bias;
+    ep.hIn = static_cast<uint16_t*>(hIn);
+    ep.hPost = hPostNext;
+    ep.hRes = hResNext;
+    return bf ? launch_epi<MHC_DTYPE_BF16, kPostPreNS>(p, ep, stream) : launch_epi<MHC_DTYPE_F16, kPostPreNS>(p, ep, stream);
 }
 
 // ---------------------------------------------------------------------------
