@@ -76,6 +76,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--batch", type=int, default=0, help="override the config's batch (profiling cases)")
     ap.add_argument("--decode-sweep", action="store_true", help="config 5 latency sweep (its own JSON line)")
+    ap.add_argument("--post-pre", action="store_true",
+                    help="post step + next MhcPre, fused (mhcPostPreRun) against two calls (its own JSON line)")
     ap.add_argument("--post", action="store_true",
                     help="the mHC post step (mhcPostRun) at the config's shape (its own JSON line, one GPU)")
     ap.add_argument("--path", type=int, default=-1, help="plan option: force a path (default: the library's)")
@@ -413,6 +415,72 @@ def post_step(args):
         "clocks": clocks.summary()}), flush=True)
 
 
+def post_pre_step(args):
+    """One layer boundary at the config's shape on one GPU: the post step of the layer
+    that ends followed by the next layer's MhcPre, fused (mhcPostPreRun) and as two
+    calls (mhcPostRun, then mhcPreRunPrepared), back to back, CUDA events around K
+    steps of each.  Reports both times and the bytes each moves: the fused path writes
+    xNext once and reads it once; the two calls write it once and read it twice."""
+    import torch
+    import mhcpre_review_b200 as mp
+    from mhcpre_review_b200.configs import CONFIGS, make_inputs, with_shape
+    torch.cuda.set_device(0)
+    cfg = CONFIGS[args.config]
+    if args.batch > 0:
+        cfg = with_shape(cfg, batch=args.batch, name=f"{cfg.name}_b{args.batch}")
+    inp = make_inputs(cfg)
+    x = inp["x"]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(cfg.seed * 1000003 + 13)
+    y = torch.randn((cfg.batch, cfg.seq, cfg.D), generator=g, device="cuda", dtype=x.dtype)
+    hPost = (2.0 * torch.sigmoid(torch.randn((cfg.batch, cfg.seq, cfg.n), generator=g, device="cuda"))).contiguous()
+    hRes = (0.5 * torch.randn((cfg.batch, cfg.seq, cfg.n, cfg.n), generator=g, device="cuda")).contiguous()
+    ex = mp.MhcPre(cfg.batch, cfg.seq, cfg.n, cfg.D, x.dtype, cfg.gamma, cfg.norm_eps, cfg.hc_eps)
+    ex.prepare(inp["phi"], inp["gamma"])
+    out = ex.outputs(x.dtype)
+    xn = torch.empty_like(x)
+
+    def fused():
+        ex.post_and_run(x, y, hPost, hRes, inp["alpha"], inp["bias"], x_next=xn, out=out)
+
+    def separate():
+        mp.mhc_post(x, y, hPost, hRes, out=xn)
+        ex(xn, inp["alpha"], inp["bias"], out=out)
+
+    res = {}
+    with ClockSampler(0) as clocks:
+        for name, fn in (("separate", separate), ("fused", fused)):
+            for _ in range(max(args.warmup, 3)):
+                fn()
+            torch.cuda.synchronize()
+            b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b.record()
+            for _ in range(args.steps):
+                fn()
+            e.record()
+            torch.cuda.synchronize()
+            res[name] = b.elapsed_time(e) / args.steps
+    if mp.device_status() != 0:
+        raise RuntimeError("device status")
+    M, n, D = cfg.M, cfg.n, cfg.D
+    xb, yb, hb = M * n * D * 2, M * D * 2, M * D * 2
+    coef = M * (n + n * n) * 4
+    fused_bytes = (xb + yb + coef + xb) + (xb + hb + coef)       # post in and out; the hIn pass; outputs
+    separate_bytes = fused_bytes + xb                             # plus the first MhcPre pass reading xNext
+    peak, kind = measured_peaks()
+    print(json.dumps({
+        "metric": "mHC layer boundary: post step + next MhcPre, fused vs two calls", "unit": "ms per step",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+        "dtype": cfg.dtype, "data": "synthetic (seeded)",
+        "config": {"workload": f"{cfg.name} shape: M={M}, n={n}, D={D}, {cfg.dtype}",
+                   "l2": "inputs larger than L2, no flush"},
+        "fused_ms": res["fused"], "separate_ms": res["separate"], "speedup": res["separate"] / res["fused"],
+        "fused_bytes": fused_bytes, "separate_bytes": separate_bytes,
+        "fused_GBps_of_its_bytes": fused_bytes / (res["fused"] * 1e-3) / 1e9,
+        "separate_GBps_of_its_bytes": separate_bytes / (res["separate"] * 1e-3) / 1e9,
+        "peak_GBps": peak, "peak_kind": kind, "clocks": clocks.summary()}), flush=True)
+
+
 def decode_sweep(args):
     """p50 latency per M, flushed and unflushed L2 (own JSON line)."""
     import torch
@@ -602,6 +670,9 @@ def main():
         return
     if args.post:
         post_step(args)
+        return
+    if args.post_pre:
+        post_pre_step(args)
         return
     world, rank, local = dist_env()
     from mhcpre_review_b200.configs import CONFIGS, with_shape as _ws

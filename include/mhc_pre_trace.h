@@ -3,7 +3,8 @@
  *
  * The trace build is the operator library compiled with -DMHC_TRACE: the same
  * entry points (include/mhc_pre.h) and the same results, plus, in the kernels of
- * the split-K path (0) and the one-pass path (5), %globaltimer stamps of their
+ * the split-K path (0), the one-pass path (5) and the fused post step
+ * (mhcPostPreRun), %globaltimer stamps of their
  * stages, recorded by every 8th CTA into a device array of 4 Mi records.  The
  * default library exports none of this and records nothing.  No reference
  * counterpart (the reference's own notes propose GetSystemCycle stage markers,
@@ -18,7 +19,9 @@
  *                 5 row's tile complete, 6 row's records summed, 7 row's hIn
  *                 written (one-pass path), 8 / 9 split-K epilogue row begin / end
  *                 (a = row low 32 bits, b = row high 32 bits); 10 / 11 CTA begin /
- *                 end (a = path)
+ *                 end (a = path).  In the fused post + MhcPre kernel (mhcPostPreRun):
+ *                 2 a stage's loads issued, 5 its data landed, 6 its xNext formed,
+ *                 7 its xNext stores have read it (a = the CTA's stage count, b = tile)
  *   uint32 a, b   event arguments
  */
 #ifndef MHC_PRE_TRACE_H

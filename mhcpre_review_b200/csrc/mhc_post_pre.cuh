@@ -8,7 +8,7 @@
 //   producer warp   TMA: for one 64-wide d-chunk of a 128-row tile, the x tiles of
 //                   all n streams, the y tile, and the n chunks of the next layer's
 //                   prepared weights that meet those K positions (k = s*D + d).
-//   post warps 4-11 each thread owns half of a row's 16-byte pieces: it reads the n
+//   post warps 4-19 each thread owns a quarter of a row's 16-byte pieces: it reads the n
 //                   x pieces and the y piece, forms the n xNext pieces in the post
 //                   step's operation order (mhc_post.cuh), writes them back over the
 //                   x pieces (the stage then holds xNext in the TMA layout), and adds
@@ -59,7 +59,21 @@ struct PostPreParams {
     const WorkspaceHeader* hdr;
 };
 
-constexpr int kPostPreThreads = 384;  // 12 warps
+constexpr int kPostPreThreads = 640;  // 20 warps: producer, MMA, stores, spare, 16 post warps
+constexpr int kPostPreWarps = 16;     // post warps: four per row quarter, each two of a row's eight 16-byte pieces
+
+// Rounds two fp32 values to the 16-bit dtype (nearest even) in one conversion; the
+// same bits as f32x2_to_x2.
+template <int DT>
+__device__ __forceinline__ uint32_t f32x2_to_x2_packed(float a, float b) {
+    if constexpr (DT == MHC_DTYPE_BF16) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    } else {
+        const __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+}
 constexpr int kPostPreNS = 4;
 constexpr int kPostPreN = 2 * (kPostPreNS * kPostPreNS + 2 * kPostPreNS);  // 48
 constexpr int kPostPreTile = kRowsPerTile * kChunk * 2;                        // 16 KB
@@ -82,12 +96,12 @@ __global__ void __launch_bounds__(kPostPreThreads, 1)
     const int S = p.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * kPostPreStage);  // [S]
     uint64_t* empty = full + S;        // [S] MMA commit + store thread
-    uint64_t* postDone = empty + S;    // [S] the eight post warps
+    uint64_t* postDone = empty + S;    // [S] the post warps
     uint64_t* accFull = postDone + S;  // [2]
     uint64_t* accEmpty = accFull + 2;  // [2] the four flush warps
     uint32_t* tmemSlot = reinterpret_cast<uint32_t*>(accEmpty + 2);
     volatile int* abortFlag = reinterpret_cast<volatile int*>(tmemSlot + 1);
-    float* sSumsq = reinterpret_cast<float*>(smem + static_cast<size_t>(S) * kPostPreStage + 256);  // [128]
+    float* sSumsq = reinterpret_cast<float*>(smem + static_cast<size_t>(S) * kPostPreStage + 256);  // [3][128]
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -109,7 +123,7 @@ __global__ void __launch_bounds__(kPostPreThreads, 1)
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 2);
-            mbar_init(&postDone[s], 8);
+            mbar_init(&postDone[s], kPostPreWarps);
         }
         for (int b = 0; b < kAccBufs; ++b) {
             mbar_init(&accFull[b], 1);
@@ -156,6 +170,7 @@ __global__ void __launch_bounds__(kPostPreThreads, 1)
                             break;
                         }
                         const int d0 = (cBegin + i) * kChunk;
+                        MHC_TRACE_EV(kTrGemmItemIssue, g, tile);
                         mbar_arrive_expect_tx(&full[s], kPostPreStage);
                         for (int t = 0; t < NS; ++t) {
                             const int k0 = static_cast<int>(t * p.D) + d0;
@@ -231,17 +246,18 @@ __global__ void __launch_bounds__(kPostPreThreads, 1)
                         bulk_commit_group();
                         bulk_wait_group_read0();  // the stage may be refilled once the stores have read it
                         mbar_arrive(&empty[s]);
+                        MHC_TRACE_EV(kTrRowDone, g, tile);
                     }
                 }
                 bulk_wait_group0();  // every xNext store is complete before the CTA ends
             }
         } else if (warp >= 4) {
             // ---------------- post step, square-sum, flush, records ----------------
-            const int pw = warp - 4;         // 0..7
+            const int pw = warp - 4;         // 0..15
             const int q = pw & 3;            // row quarter = TMEM lane quadrant
-            const int half = pw >> 2;        // pieces [4*half, 4*half + 4) of a row
+            const int part = pw >> 2;        // pieces [2*part, 2*part + 2) of a row
             const int row = q * 32 + lane;
-            const bool flusher = half == 0;  // warps 4-7 hold run[] and write records
+            const bool flusher = part == 0;  // warps 4-7 hold run[] and write records
             const uint32_t lane_base = tacc + (static_cast<uint32_t>(q * 32) << 16);
             const float unscale = ldexpf(1.0f, -p.hdr->phiScaleExp);
             float run[MIX];
@@ -279,13 +295,14 @@ __global__ void __launch_bounds__(kPostPreThreads, 1)
                         itemOk = false;
                         break;
                     }
+                    if (pw == 0 && lane == 0) MHC_TRACE_EV(kTrRowReady, g, tile);
                     const uint32_t yBase = smem_u32(tile_y(s)) + row * 128;
                     uint32_t xBase[NS];
 #pragma unroll
                     for (int t = 0; t < NS; ++t) xBase[t] = smem_u32(tile_x(s, t)) + row * 128;
 #pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) {
-                        const int j = half * 4 + jj;                 // 16-byte piece of the 128-byte row
+                    for (int jj = 0; jj < 2; ++jj) {
+                        const int j = part * 2 + jj;                 // 16-byte piece of the 128-byte row
                         const uint32_t off = static_cast<uint32_t>((j ^ (row & 7)) << 4);  // 128-byte swizzle
                         uint4 xv[NS];
 #pragma unroll
@@ -314,7 +331,7 @@ __global__ void __launch_bounds__(kPostPreThreads, 1)
                                 }
                                 a = __fmaf_rn(post[o], yf.x, a);
                                 c = __fmaf_rn(post[o], yf.y, c);
-                                const uint32_t packed = f32x2_to_x2<DT>(a, c);
+                                const uint32_t packed = f32x2_to_x2_packed<DT>(a, c);
                                 ow[o][qq] = packed;
                                 // the next MhcPre's square-sum, of the rounded xNext
                                 const float2 r = x2_to_f32<DT>(packed);
@@ -330,6 +347,7 @@ __global__ void __launch_bounds__(kPostPreThreads, 1)
                     fence_proxy_async();  // the MMA and the TMA stores read these writes
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&postDone[s]);
+                    if (pw == 0 && lane == 0) MHC_TRACE_EV(kTrRowReduced, g, tile);
                     // the previous d-chunk's segment (its MMA finished while this one's
                     // post step ran) into registers
                     if (flusher && i >= 1 && !flush(g - 1)) {
@@ -337,16 +355,17 @@ __global__ void __launch_bounds__(kPostPreThreads, 1)
                         break;
                     }
                 }
-                // the item's last segment; the two halves of each row's sum of squares.
+                // the item's last segment; the four parts of each row's sum of squares.
                 // Every post warp takes both barriers once per item, also after a wait
                 // gave up (the abort flag then ends every other wait promptly), so the
                 // barriers always match.
                 if (flusher && itemOk) itemOk = flush(g - 1);
-                if (!flusher) sSumsq[row] = ss;
-                named_bar_sync(1, 256);
-                const bool anyFailed = bar_red_or(2, 256, !itemOk);
+                if (!flusher) sSumsq[(part - 1) * kRowsPerTile + row] = ss;
+                named_bar_sync(1, kPostPreWarps * 32);
+                const bool anyFailed = bar_red_or(2, kPostPreWarps * 32, !itemOk);
                 if (!anyFailed && flusher) {
-                    const float ssRow = ss + sSumsq[row];
+                    const float ssRow =
+                        ((ss + sSumsq[row]) + sSumsq[kRowsPerTile + row]) + sSumsq[2 * kRowsPerTile + row];
                     const int64_t recAt = (static_cast<int64_t>(split) * p.M + grow) * p.W;
                     if (grow < p.M && MHC_CHECK(split < p.splits && recAt + MIX < p.partFloats)) {
                         float* out = p.partials + recAt;
@@ -362,7 +381,7 @@ __global__ void __launch_bounds__(kPostPreThreads, 1)
                         out[MIX] = ssRow;
                     }
                 }
-                named_bar_sync(1, 256);  // sSumsq is free for the next item
+                named_bar_sync(1, kPostPreWarps * 32);  // sSumsq is free for the next item
                 if (anyFailed) ok = false;
             }
             if (!ok && lane == 0) fail();

@@ -101,7 +101,7 @@ constexpr size_t kPostPreStageBytesHost = 5 * static_cast<size_t>(kRowsPerTile) 
 constexpr int kPostPreStages = 2;
 constexpr size_t post_pre_smem_bytes(int stages) {
     return 1024 /*alignment slack*/ + static_cast<size_t>(stages) * kPostPreStageBytesHost + 256 /*barriers*/ +
-           128 * 4 /*sums of squares*/;
+           3 * 128 * 4 /*partial sums of squares*/;
 }
 struct PostPrePlan {
     int tilesM, dChunks, splits, stages, grid;
