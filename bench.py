@@ -85,6 +85,8 @@ def parse():
     ap.add_argument("--ctas", type=int, default=0, help="plan option: GEMM CTAs per SM")
     ap.add_argument("--stages", type=int, default=0, help="plan option: TMA ring depth")
     ap.add_argument("--ring", type=int, default=0, help="plan option: one-pass record ring slots")
+    ap.add_argument("--epi-blocks", type=int, default=0,
+                    help="plan option: split-K epilogue rows resident per SM (12 or 16)")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the configs 2, 3 and 5 measurements the default one-GPU run adds to its line")
     ap.add_argument("--no-flush", action="store_true",
@@ -698,9 +700,9 @@ def main():
 
     import mhcpre_review_b200 as mp
     from mhcpre_review_b200.configs import make_inputs, with_shape
-    if args.path >= 0 or args.splits or args.ctas or args.stages or args.ring:
+    if args.path >= 0 or args.splits or args.ctas or args.stages or args.ring or args.epi_blocks:
         mp._OPTIONS = mp.make_plan_options(path=args.path, splits=args.splits, gemm_ctas_per_sm=args.ctas,
-                                           gemm_stages=args.stages, ring_tiles=args.ring)
+                                           gemm_stages=args.stages, ring_tiles=args.ring, epi_blocks=args.epi_blocks)
 
     # every rank generates the same batch (same seeds) and keeps its contiguous rows;
     # the weights are replicated

@@ -205,7 +205,9 @@ typedef struct {
     int32_t ringTiles;     /* one-pass path: tile slots of the partial-record ring */
     int32_t pairedGemm;    /* split-K path at n = 8: 0 the library's choice, 1 one-CTA GEMM,
                               2 GEMM on CTA pairs (one M = 256 tcgen05 MMA per pair) */
-    int32_t reserved[6];   /* must be 0 */
+    int32_t epiBlocks;     /* split-K path: epilogue rows resident per SM, 0 the library's
+                              choice (16 up to 16384 rows, else 12), 12 or 16 */
+    int32_t reserved[5];   /* must be 0 */
 } mhcPrePlanOptions_t;
 
 /* mhcPreGetWorkspaceSize / mhcPreQueryPlan / mhcPrePrepareWeights /

@@ -76,13 +76,14 @@ class MhcPrePlanOptions(ctypes.Structure):
     _fields_ = [("path", ctypes.c_int32), ("splits", ctypes.c_int32), ("gemmCtasPerSm", ctypes.c_int32),
                 ("gemmStages", ctypes.c_int32), ("tmaBatch", ctypes.c_int32), ("teamSize", ctypes.c_int32),
                 ("clusterLead", ctypes.c_int32), ("l2Hint", ctypes.c_int32), ("ringTiles", ctypes.c_int32),
-                ("pairedGemm", ctypes.c_int32), ("reserved", ctypes.c_int32 * 6)]
+                ("pairedGemm", ctypes.c_int32), ("epiBlocks", ctypes.c_int32), ("reserved", ctypes.c_int32 * 5)]
 
 
 def make_plan_options(path=PATH_AUTO, splits=0, gemm_ctas_per_sm=0, gemm_stages=0, tma_batch=0, team_size=0,
-                      cluster_lead=0, l2_hint=0, ring_tiles=0, paired_gemm=0) -> MhcPrePlanOptions:
+                      cluster_lead=0, l2_hint=0, ring_tiles=0, paired_gemm=0, epi_blocks=0) -> MhcPrePlanOptions:
     return MhcPrePlanOptions(int(path), int(splits), int(gemm_ctas_per_sm), int(gemm_stages), int(tma_batch),
-                             int(team_size), int(cluster_lead), int(l2_hint), int(ring_tiles), int(paired_gemm))
+                             int(team_size), int(cluster_lead), int(l2_hint), int(ring_tiles), int(paired_gemm),
+                             int(epi_blocks))
 
 
 # Plan options every call of this module passes to the library (None: the default

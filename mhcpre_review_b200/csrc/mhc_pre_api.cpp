@@ -70,7 +70,7 @@ constexpr int64_t kShardRows = 8192;  // from this M up, splits depend on K only
 constexpr int kMinSplitChunks = 6;    // smallest split below kShardRows rows
 
 int make_plan(const Problem& p, int smCount, const mhcPrePlanOptions_t* opt, Plan* plan) {
-    static const mhcPrePlanOptions_t kDefaults = {MHC_PRE_PATH_AUTO, 0, 0, 0, 0, 0, 0, 0, 0, 0, {0, 0, 0, 0, 0, 0}};
+    static const mhcPrePlanOptions_t kDefaults = {MHC_PRE_PATH_AUTO, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, {0, 0, 0, 0, 0}};
     const mhcPrePlanOptions_t& o = opt != nullptr ? *opt : kDefaults;
     const bool autoPath = o.path == MHC_PRE_PATH_AUTO;
     Plan pl{};
@@ -122,6 +122,7 @@ int make_plan(const Problem& p, int smCount, const mhcPrePlanOptions_t* opt, Pla
     // so the same result bits): items are (256-row pair tile, split), one pair per
     // SM's worth of CTA slots, four 26 KB stages per CTA.
     pl.pairGemm = p.N == 160 && o.pairedGemm == 2;
+    pl.epiBlocks = o.epiBlocks != 0 ? o.epiBlocks : p.M <= kEpiWideMaxRows ? 16 : 12;
     if (pl.pairGemm) {
         const int pairTiles = (pl.tilesM + 1) / 2;
         pl.stages = std::max(2, std::min(o.gemmStages > 0 ? o.gemmStages : 4, 4));
@@ -377,6 +378,7 @@ static int options_ok(const mhcPrePlanOptions_t* opt) {
     if (opt == nullptr) return MHC_STATUS_SUCCESS;
     if (opt->path < MHC_PRE_PATH_AUTO || opt->path > 5) return MHC_STATUS_BAD_SHAPE;
     if (opt->pairedGemm < 0 || opt->pairedGemm > 2) return MHC_STATUS_BAD_SHAPE;
+    if (opt->epiBlocks != 0 && opt->epiBlocks != 12 && opt->epiBlocks != 16) return MHC_STATUS_BAD_SHAPE;
     for (int r : opt->reserved)
         if (r != 0) return MHC_STATUS_BAD_SHAPE;
     return MHC_STATUS_SUCCESS;

@@ -92,7 +92,12 @@ struct Plan {
     int opCtasPerSm;
     // path 0 at n = 8: the GEMM runs on CTA pairs (one M = 256 MMA, cta_group::2)
     bool pairGemm;
+    // path 0: epilogue blocks (rows) resident per SM the epilogue is compiled for, 12
+    // or 16; 16 takes fewer registers per thread and keeps more rows in flight, which
+    // pays where the epilogue is latency-bound (up to kEpiWideMaxRows rows)
+    int epiBlocks;
 };
+constexpr int64_t kEpiWideMaxRows = 16384;
 
 // The post step fused with the next MhcPre's contraction (n = 4, D % 64 == 0): a stage
 // holds the x tiles of the 4 streams and the y tile of one 64-wide d-chunk (16 KB

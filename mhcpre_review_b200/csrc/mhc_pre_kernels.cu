@@ -478,6 +478,7 @@ struct EpiParams {
     uint16_t* hIn;
     float* hPost;
     float* hRes;
+    int blocksPerSm;  // 12 or 16: the epilogue variant
 };
 
 constexpr int kEpiThreads = 128;
@@ -497,8 +498,10 @@ __device__ __forceinline__ float sigmoid_ref(float v) {
 // Launched as a programmatic dependent of the GEMM: it waits for the GEMM's
 // completion (and memory) before reading the partial records.  Dynamic shared
 // memory: min(splits, kEpiSplitBlock) * (mix + 1) floats.
-template <int DT, int NS>
-__global__ void __launch_bounds__(kEpiThreads) epilogue_hin_kernel(const EpiParams p) {
+// BLOCKS: resident blocks per SM it is compiled for (12: 40 registers a thread; 16:
+// at most 32).  The arithmetic does not depend on it.
+template <int DT, int NS, int BLOCKS>
+__global__ void __launch_bounds__(kEpiThreads, BLOCKS) epilogue_hin_kernel(const EpiParams p) {
     constexpr int mix = NS * NS + 2 * NS;
     constexpr int cols = mix + 1;
     extern __shared__ float sPart[];  // [block split][cols]
@@ -724,7 +727,8 @@ static int launch_epi(const Problem& p, const EpiParams& ep, cudaStream_t stream
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, epilogue_hin_kernel<DT, NS>, ep);
+    return cudaLaunchKernelEx(&cfg, ep.blocksPerSm == 16 ? epilogue_hin_kernel<DT, NS, 16> : epilogue_hin_kernel<DT, NS, 12>,
+                              ep);
 }
 
 template <int DT, int NS>
@@ -1177,6 +1181,7 @@ int launch_run(const Problem& p, const Plan& plan, const CUtensorMap& xMap, cons
     ep.hcEps = p.hcEps;
     ep.partials = gp.partials;
     ep.partFloats = gp.partFloats;
+    ep.blocksPerSm = plan.epiBlocks;
     ep.x = static_cast<const uint16_t*>(x);
     ep.alpha = alpha;
     ep.bias = bias;
@@ -1265,6 +1270,7 @@ int launch_post_pre(const Problem& p, const PostPrePlan& pp, const Plan& plan, c
     ep.hcEps = p.hcEps;
     ep.partials = prm.partials;
     ep.partFloats = prm.partFloats;
+    ep.blocksPerSm = plan.epiBlocks;
     ep.x = static_cast<const uint16_t*>(xNext);
     ep.alpha = alpha;
     ep.bias = bias;

@@ -107,6 +107,8 @@ def test_plan_options_are_validated_before_the_device():
     bad = mp.make_plan_options()
     bad.reserved[3] = 1
     assert mp.lib().mhcPreGetWorkspaceSizeEx(ctypes.byref(desc), ctypes.byref(bad), ctypes.byref(n)) == -2
+    bad = mp.make_plan_options(epi_blocks=8)  # 12 or 16 only
+    assert mp.lib().mhcPreGetWorkspaceSizeEx(ctypes.byref(desc), ctypes.byref(bad), ctypes.byref(n)) == -2
 
 
 def test_library_reads_no_environment():
