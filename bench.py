@@ -85,6 +85,8 @@ def parse():
     ap.add_argument("--ctas", type=int, default=0, help="plan option: GEMM CTAs per SM")
     ap.add_argument("--stages", type=int, default=0, help="plan option: TMA ring depth")
     ap.add_argument("--ring", type=int, default=0, help="plan option: one-pass record ring slots")
+    ap.add_argument("--paired", type=int, default=0,
+                    help="plan option: n = 8 GEMM layout (1 one CTA, 2 CTA pairs)")
     ap.add_argument("--epi-blocks", type=int, default=0,
                     help="plan option: split-K epilogue rows resident per SM (12 or 16)")
     ap.add_argument("--no-extra", action="store_true",
@@ -700,9 +702,10 @@ def main():
 
     import mhcpre_review_b200 as mp
     from mhcpre_review_b200.configs import make_inputs, with_shape
-    if args.path >= 0 or args.splits or args.ctas or args.stages or args.ring or args.epi_blocks:
+    if args.path >= 0 or args.splits or args.ctas or args.stages or args.ring or args.epi_blocks or args.paired:
         mp._OPTIONS = mp.make_plan_options(path=args.path, splits=args.splits, gemm_ctas_per_sm=args.ctas,
-                                           gemm_stages=args.stages, ring_tiles=args.ring, epi_blocks=args.epi_blocks)
+                                           gemm_stages=args.stages, ring_tiles=args.ring, epi_blocks=args.epi_blocks,
+                                           paired_gemm=args.paired)
 
     # every rank generates the same batch (same seeds) and keeps its contiguous rows;
     # the weights are replicated
