@@ -88,3 +88,42 @@ def test_wrong_outputs_are_rejected():
     out = (torch.empty(1, 8, 64, dtype=torch.bfloat16), torch.empty(1, 8, 4), torch.empty(1, 8, 4, 3))
     with pytest.raises(mp.MhcPreError, match="hRes"):
         mp._check_run(desc(), CPU, a["x"], a["alpha"], a["bias"], out)
+
+
+def _cpu_executor(d):
+    """An executor object pinned to the CPU device, without a workspace: enough for
+    the argument checks, which all run before any call into the library."""
+    ex = object.__new__(mp.MhcPre)
+    ex.desc = d
+    ex.device = CPU
+    return ex
+
+
+def _post_pre_args():
+    a = good()
+    return dict(x=a["x"], y=torch.zeros(1, 8, 64, dtype=torch.bfloat16), hPost=torch.zeros(1, 8, 4),
+                hRes=torch.zeros(1, 8, 4, 4), alpha=a["alpha"], bias=a["bias"])
+
+
+@pytest.mark.parametrize("field,bad,msg", [
+    ("y", torch.zeros(1, 8, 64, dtype=torch.float16), "dtype"),
+    ("y", torch.zeros(1, 8, 48, dtype=torch.bfloat16), "elements"),
+    ("y", torch.zeros(1, 64, 8, dtype=torch.bfloat16).transpose(1, 2), "contiguous"),
+    ("hPost", torch.zeros(1, 8, 4, dtype=torch.float64), "dtype"),
+    ("hRes", torch.zeros(1, 8, 4, 3), "elements"),
+    ("x", torch.zeros(1, 8, 4, 32, dtype=torch.bfloat16), "elements"),
+    ("alpha", torch.ones(2), "elements"),
+])
+def test_post_and_run_rejects_bad_arguments(field, bad, msg):
+    """MhcPre.post_and_run (mhcPostPreRun) checks the ending layer's y, hPost and
+    hRes as well as the next layer's run arguments."""
+    args = _post_pre_args()
+    args[field] = bad
+    with pytest.raises(mp.MhcPreError, match=msg):
+        _cpu_executor(desc()).post_and_run(**args)
+
+
+def test_post_and_run_rejects_a_wrong_x_next():
+    args = _post_pre_args()
+    with pytest.raises(mp.MhcPreError, match="elements"):
+        _cpu_executor(desc()).post_and_run(**args, x_next=torch.zeros(1, 8, 4, 32, dtype=torch.bfloat16))
