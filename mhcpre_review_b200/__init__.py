@@ -306,10 +306,50 @@ def _check_run(desc, device, x, alpha, bias, out=None):
         _require(hRes, "hRes", device, torch.float32, (desc.batch, desc.seq, desc.streams, desc.streams))
 
 
+def _args_ok(tensors, specs, device_index) -> bool:
+    """Fast form of the argument checks for a hot call: every tensor has its expected
+    dtype and element count, is dense and sits on the executor's device.  False sends
+    the call through the full checks, which raise with the reason."""
+    try:
+        for t, (dtype, numel) in zip(tensors, specs):
+            if t.dtype != dtype or t.numel() != numel or t.get_device() != device_index or not t.is_contiguous():
+                return False
+        return True
+    except AttributeError:  # not a tensor
+        return False
+
+
 def _stream_ptr(stream):
-    torch = _torch()
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return ctypes.c_void_p(s.cuda_stream)
+    """The cudaStream_t to launch on: the given torch stream, else torch's current
+    stream on the current device (read as a raw handle, without building a Stream
+    object, which costs more host time than the launch itself)."""
+    if stream is not None:
+        return ctypes.c_void_p(stream.cuda_stream)
+    C = _torch()._C
+    return ctypes.c_void_p(C._cuda_getCurrentRawStream(C._cuda_getDevice()))
+
+
+class _on_device:
+    """``with _on_device(dev): ...`` makes the CUDA device dev current for the enclosed
+    calls (the library plans and launches on the current device) and restores the
+    previous one afterwards; it switches nothing when dev is already current."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device):
+        self.idx = device.index
+
+    def __enter__(self):
+        C = _torch()._C
+        self.prev = C._cuda_getDevice()
+        if self.prev != self.idx:
+            C._cuda_setDevice(self.idx)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev != self.idx:
+            _torch()._C._cuda_setDevice(self.prev)
+        return False
 
 
 class MhcPre:
@@ -335,6 +375,14 @@ class MhcPre:
                 raise MhcPreError(-8, "workspace")
         self.workspace = workspace
         self.prepared = False
+        # expected (dtype, elements) of x, alpha, bias, hIn, hPost, hRes for _args_ok
+        d = self.desc
+        x_dtype = torch.bfloat16 if d.dtype == BF16 else torch.float16
+        mix = d.streams * d.streams + 2 * d.streams
+        self._run_specs = ((x_dtype, d.batch * d.seq * d.streams * d.headDim), (torch.float32, 3),
+                           (torch.float32, mix), (x_dtype, d.batch * d.seq * d.headDim),
+                           (torch.float32, d.batch * d.seq * d.streams),
+                           (torch.float32, d.batch * d.seq * d.streams * d.streams))
 
     @property
     def plan(self) -> dict:
@@ -343,7 +391,7 @@ class MhcPre:
     def prepare(self, phi, gamma=None, stream=None):
         torch = _torch()
         _check_weights(self.desc, self.device, phi, gamma)
-        with torch.cuda.device(self.device):
+        with _on_device(self.device):
             _check(lib().mhcPrePrepareWeightsEx(ctypes.byref(self.desc), _opt(), _ptr(phi), _ptr(gamma),
                                                 _ptr(self.workspace), self.ws_bytes, _stream_ptr(stream)),
                    "PrepareWeights")
@@ -362,7 +410,7 @@ class MhcPre:
         torch = _torch()
         _check_run(self.desc, self.device, x, alpha, bias, out)
         hIn, hPost, hRes = out
-        with torch.cuda.device(self.device):
+        with _on_device(self.device):
             _check(lib().mhcPreRunPreparedEx(ctypes.byref(self.desc), _opt(), _ptr(x), _ptr(alpha), _ptr(bias),
                                              _ptr(hIn), _ptr(hPost), _ptr(hRes), _ptr(self.workspace),
                                              self.ws_bytes, _stream_ptr(stream),
@@ -387,17 +435,18 @@ class MhcPre:
             x_next = torch.empty_like(x)
         _check_run(d, self.device, x_next, alpha, bias, out)
         hIn, hPostN, hResN = out if out is not None else self.outputs(x_dtype)
-        with torch.cuda.device(self.device):
+        with _on_device(self.device):
             _check(lib().mhcPostPreRun(ctypes.byref(d), _ptr(x), _ptr(y), _ptr(hPost), _ptr(hRes), _ptr(x_next),
                                        _ptr(alpha), _ptr(bias), _ptr(hIn), _ptr(hPostN), _ptr(hResN),
                                        _ptr(self.workspace), self.ws_bytes, _stream_ptr(stream)), "PostPreRun")
         return x_next, (hIn, hPostN, hResN)
 
     def __call__(self, x, alpha, bias, out=None, stream=None):
-        torch = _torch()
-        _check_run(self.desc, self.device, x, alpha, bias, out)
+        args = (x, alpha, bias) if out is None else (x, alpha, bias, *out)
+        if not _args_ok(args, self._run_specs, self.device.index):
+            _check_run(self.desc, self.device, x, alpha, bias, out)
         hIn, hPost, hRes = out if out is not None else self.outputs(x.dtype)
-        with torch.cuda.device(self.device):
+        with _on_device(self.device):
             if _OPTIONS is None:
                 rc = lib().mhcPreRunPrepared(ctypes.byref(self.desc), _ptr(x), _ptr(alpha), _ptr(bias), _ptr(hIn),
                                              _ptr(hPost), _ptr(hRes), _ptr(self.workspace), self.ws_bytes,
@@ -421,7 +470,7 @@ def mhc_pre(x, phi, alpha, bias, gamma=None, norm_eps=1e-6, hc_eps=1e-6, out=Non
     if x.device.type != "cuda":
         raise MhcPreError(-2, f"x must be a CUDA tensor (got {x.device}); there is no CPU path")
     B, S, n, D = x.shape
-    with torch.cuda.device(x.device):
+    with _on_device(x.device):
         ex = MhcPre(B, S, n, D, x.dtype, gamma is not None, norm_eps, hc_eps, device=x.device, workspace=workspace)
         _check_weights(ex.desc, ex.device, phi, gamma)
         _check_run(ex.desc, ex.device, x, alpha, bias, out)
@@ -460,7 +509,7 @@ def mhc_post(x, y, hPost, hRes, out=None, stream=None):
         out = torch.empty_like(x)
     _require(out, "out", x.device, x.dtype, tuple(x.shape))
     desc = make_desc(B, S, n, D, _dtype_code(x.dtype), False)
-    with torch.cuda.device(x.device):
+    with _on_device(x.device):
         _check(lib().mhcPostRun(ctypes.byref(desc), _ptr(x), _ptr(y), _ptr(hPost), _ptr(hRes), _ptr(out),
                                 _stream_ptr(stream)), "PostRun")
     return out

@@ -127,3 +127,21 @@ def test_post_and_run_rejects_a_wrong_x_next():
     args = _post_pre_args()
     with pytest.raises(mp.MhcPreError, match="elements"):
         _cpu_executor(desc()).post_and_run(**args, x_next=torch.zeros(1, 8, 4, 32, dtype=torch.bfloat16))
+
+
+def test_fast_argument_check_agrees_with_the_full_one():
+    """The executor's hot-call check (_args_ok) accepts exactly what the full checks
+    accept; anything else goes through the full checks, which raise."""
+    a = good()
+    d = desc()
+    specs = ((torch.bfloat16, 1 * 8 * 4 * 64), (torch.float32, 3), (torch.float32, 24))
+    cpu = -1  # get_device() of a CPU tensor
+    assert mp._args_ok((a["x"], a["alpha"], a["bias"]), specs, cpu)
+    mp._check_run(d, CPU, a["x"], a["alpha"], a["bias"])
+    strided = torch.zeros(1, 8, 64, 4, dtype=torch.bfloat16).transpose(2, 3)
+    for bad in ((a["x"].half(), a["alpha"], a["bias"]), (a["x"], a["alpha"][:2], a["bias"]),
+                (strided, a["alpha"], a["bias"]), (a["x"], [1.0, 1.0, 1.0], a["bias"])):
+        assert not mp._args_ok(bad, specs, cpu)
+        with pytest.raises(mp.MhcPreError):
+            mp._check_run(d, CPU, *bad)
+    assert not mp._args_ok((a["x"], a["alpha"], a["bias"]), specs, 0)  # another device
