@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(kPostPreThreads, 1)
                         for (int o = 0; o < NS; ++o)
                             sts128(xBase[o] + off, make_uint4(ow[o][0], ow[o][1], ow[o][2], ow[o][3]));
                     }
-                    fence_proxy_async();  // the MMA and the TMA stores read these writes
+                    fence_proxy_async_shared();  // the MMA and the TMA stores read these shared-memory writes
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&postDone[s]);
                     if (pw == 0 && lane == 0) MHC_TRACE_EV(kTrRowReduced, g, tile);

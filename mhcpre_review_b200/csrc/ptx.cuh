@@ -121,6 +121,11 @@ __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepco
 
 // Orders this thread's generic-proxy accesses against its async-proxy (TMA/bulk) ones.
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
+// The same for shared memory only (the generic-proxy writes an MMA or a TMA store of
+// this CTA will read).
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;
