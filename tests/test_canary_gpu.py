@@ -81,3 +81,43 @@ def test_outputs_and_workspace_keep_their_guard_bands(shape, monkeypatch):
     assert ok, f"{bad} guard bytes changed"
     # the outputs were written (not left at the guard pattern)
     assert torch.isfinite(out[1]).all() and torch.isfinite(out[2]).all()
+
+
+POST_PRE_SHAPES = [  # (B, S, n, D, gamma, dtype): the fused kernel (n = 4, D % 64 == 0, > 384 rows) and a fallback
+    (1, 1000, 4, 1024, True, "bf16"),   # ragged last tile
+    (1, 700, 4, 512, False, "fp16"),
+    (1, 600, 6, 512, True, "bf16"),     # n = 6: the two calls
+]
+
+
+@pytest.mark.parametrize("shape", POST_PRE_SHAPES, ids=lambda s: f"B{s[0]}S{s[1]}n{s[2]}D{s[3]}{s[5]}")
+def test_post_pre_keeps_the_guard_bands(shape):
+    """mhcPostPreRun writes xNext (its TMA stores), the next layer's outputs and the
+    records; guard bands around each of them stay intact."""
+    B, S, n, D, g, dt = shape
+    cfg = Config("canary_pp", B, S, n, D, dt, 0.02, g, seed=62)
+    inp = make_inputs(cfg)
+    x = inp["x"]
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    y = torch.randn((B, S, D), generator=gen, device="cuda", dtype=x.dtype)
+    hPost = torch.rand((B, S, n), generator=gen, device="cuda")
+    hRes = (0.5 * torch.randn((B, S, n, n), generator=gen, device="cuda")).contiguous()
+    desc = mp.make_desc(B, S, n, D, mp.BF16 if dt == "bf16" else mp.F16, g)
+    ws_bytes = mp.workspace_size(desc)
+    M = B * S
+    gb = Guarded([M * n * D * 2, M * D * 2, M * n * 4, M * n * n * 4, ws_bytes])
+    x_next = gb.view(0, x.dtype, (B, S, n, D))
+    out = (gb.view(1, x.dtype, (B, S, D)), gb.view(2, torch.float32, (B, S, n)),
+           gb.view(3, torch.float32, (B, S, n, n)))
+    ws = gb.view(4, torch.uint8, (ws_bytes,))
+    ex = mp.MhcPre(B, S, n, D, x.dtype, g, workspace=ws)
+    ex.prepare(inp["phi"], inp["gamma"])
+    for _ in range(2):
+        ex.post_and_run(x, y, hPost, hRes, inp["alpha"], inp["bias"], x_next=x_next, out=out)
+    torch.cuda.synchronize()
+    assert mp.device_status() == 0
+    ok, bad = gb.intact()
+    assert ok, f"{bad} guard bytes changed"
+    assert torch.isfinite(out[1]).all() and torch.isfinite(out[2]).all()
+    assert torch.equal(x_next, mp.mhc_post(x, y, hPost, hRes))
