@@ -69,3 +69,47 @@ def test_debug_build_reports_a_failed_check(path, monkeypatch):
         # the context stays usable and the next call is clean
         run_op(inp, use_executor=True)
         assert mp.device_status() == 0
+
+
+def _post_pre_inputs(cfg):
+    inp = make_inputs(cfg)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(6)
+    y = torch.randn((cfg.batch, cfg.seq, cfg.D), generator=gen, device="cuda", dtype=inp["x"].dtype)
+    hPost = torch.rand((cfg.batch, cfg.seq, cfg.n), generator=gen, device="cuda")
+    hRes = (0.5 * torch.randn((cfg.batch, cfg.seq, cfg.n, cfg.n), generator=gen, device="cuda")).contiguous()
+    return inp, y, hPost, hRes
+
+
+def _post_pre(cfg, inp, y, hPost, hRes):
+    ex = mp.MhcPre(cfg.batch, cfg.seq, cfg.n, cfg.D, inp["x"].dtype, cfg.gamma)
+    ex.prepare(inp["phi"], inp["gamma"])
+    x_next, out = ex.post_and_run(inp["x"], y, hPost, hRes, inp["alpha"], inp["bias"])
+    torch.cuda.synchronize()
+    return [x_next, *out]
+
+
+def test_debug_build_fused_post_pre():
+    """The fused post + MhcPre kernel under the debug build: no check fires and the
+    results equal the default build's; with the records buffer declared too small,
+    its record writes are skipped and reported."""
+    _need_lib()
+    cfg = Config("debug_pp", 1, 1000, 4, 1024, "bf16", 0.02, True, seed=73)
+    args = _post_pre_inputs(cfg)
+    ref = _post_pre(cfg, *args)
+    with mp.use_library(mp.DEBUG_LIB_PATH) as L:
+        got = _post_pre(cfg, *args)
+        assert mp.device_status() == 0
+        line = ctypes.c_int32(-1)
+        assert L.mhcPreDebugLastCheckLine(ctypes.byref(line)) == 0 and line.value == 0
+        for u, v in zip(ref, got):
+            assert torch.equal(u, v)
+        try:
+            assert L.mhcPreDebugSetRecordCap(64) == 0
+            _post_pre(cfg, *args)
+            assert mp.device_status() == -14  # MHC_STATUS_INTERNAL_CHECK
+            assert L.mhcPreDebugLastCheckLine(ctypes.byref(line)) == 0 and line.value > 0
+        finally:
+            assert L.mhcPreDebugSetRecordCap(0) == 0
+        _post_pre(cfg, *args)
+        assert mp.device_status() == 0
