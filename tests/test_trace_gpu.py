@@ -60,3 +60,45 @@ def test_trace_build_matches_and_records_stages(path, monkeypatch):
         rows = np.array([e[r] - b[r] for r in b]) / 1e3
         print(f"\ntrace path 0 ({cfg.name}): {len(items)} traced GEMM items, {len(b)} traced epilogue rows over "
               f"{span_us:.1f} us; median epilogue row {np.median(rows):.2f} us")
+
+
+def test_trace_build_fused_post_pre_stages():
+    """The fused post + MhcPre kernel under the trace build: the same results, and per
+    traced CTA and stage the order loads issued (2) <= data landed (5) <= xNext
+    formed (6) <= xNext stores have read it (7)."""
+    if not mp.TRACE_LIB_PATH.exists():
+        pytest.fail("the trace library was not built (python -m mhcpre_review_b200.build --trace)")
+    cfg = with_shape(CONFIGS["c4"], batch=1, seq=2048, name="trace_pp")
+    inp = make_inputs(cfg)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7)
+    y = torch.randn((cfg.batch, cfg.seq, cfg.D), generator=gen, device="cuda", dtype=inp["x"].dtype)
+    hPost = torch.rand((cfg.batch, cfg.seq, cfg.n), generator=gen, device="cuda")
+    hRes = (0.5 * torch.randn((cfg.batch, cfg.seq, cfg.n, cfg.n), generator=gen, device="cuda")).contiguous()
+
+    def run():
+        ex = mp.MhcPre(cfg.batch, cfg.seq, cfg.n, cfg.D, inp["x"].dtype, cfg.gamma)
+        ex.prepare(inp["phi"], inp["gamma"])
+        x_next, out = ex.post_and_run(inp["x"], y, hPost, hRes, inp["alpha"], inp["bias"])
+        torch.cuda.synchronize()
+        return [x_next, *out]
+
+    ref = run()
+    with mp.use_library(mp.TRACE_LIB_PATH):
+        mp.trace_read()
+        got = run()
+        tr, n = mp.trace_read()
+        assert mp.device_status() == 0
+    for u, v in zip(ref, got):
+        assert torch.equal(u, v), "the trace build changed a result"
+    stamps = {}
+    for ev in (2, 5, 6, 7):
+        sel = tr[tr["event"] == ev]
+        stamps[ev] = {(int(c), int(a)): int(t) for c, a, t in zip(sel["cta"], sel["a"], sel["t_ns"])}
+    keys = set(stamps[2]) & set(stamps[5]) & set(stamps[6]) & set(stamps[7])
+    assert len(keys) > 0 and set(stamps[6]) == set(stamps[7]) == keys
+    for k in keys:
+        assert stamps[2][k] <= stamps[5][k] <= stamps[6][k] <= stamps[7][k]
+    med = lambda a, b: np.median([stamps[b][k] - stamps[a][k] for k in keys]) / 1e3
+    print(f"\ntrace fused post+pre ({cfg.name}): {len(keys)} traced stages; median us: loads to landed "
+          f"{med(2, 5):.2f}, post {med(5, 6):.2f}, stores read {med(6, 7):.2f}")
