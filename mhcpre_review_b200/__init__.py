@@ -485,6 +485,24 @@ def mhc_pre(x, phi, alpha, bias, gamma=None, norm_eps=1e-6, hc_eps=1e-6, out=Non
     return hIn, hPost, hRes
 
 
+def mhc_post_pre(x, y, hPost, hRes, phi, alpha, bias, gamma=None, norm_eps=1e-6, hc_eps=1e-6, x_next=None,
+                 out=None, workspace=None, stream=None):
+    """One-shot layer boundary: the ending layer's post step (x, y, hPost, hRes) fused
+    with the next layer's MhcPre (phi, alpha, bias, gamma), i.e. the weights are
+    prepared, then mhcPostPreRun.  Returns (x_next, (hIn, hPost, hRes)) of the next
+    layer; x_next may be x."""
+    torch = _torch()
+    if not isinstance(x, torch.Tensor) or x.dim() != 4:
+        raise MhcPreError(-2, "x must be a 4-D tensor [B, S, n, D]")
+    if x.device.type != "cuda":
+        raise MhcPreError(-2, f"x must be a CUDA tensor (got {x.device}); there is no CPU path")
+    B, S, n, D = x.shape
+    with _on_device(x.device):
+        ex = MhcPre(B, S, n, D, x.dtype, gamma is not None, norm_eps, hc_eps, device=x.device, workspace=workspace)
+        ex.prepare(phi, gamma, stream)
+        return ex.post_and_run(x, y, hPost, hRes, alpha, bias, x_next=x_next, out=out, stream=stream)
+
+
 def mhc_post(x, y, hPost, hRes, out=None, stream=None):
     """The mHC post step after the layer: xNext[..., s, :] = sum_t hRes[..., s, t] *
     x[..., t, :] + hPost[..., s] * y[..., :].  x: [B, S, n, D] fp16/bf16 CUDA tensor

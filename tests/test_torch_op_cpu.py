@@ -24,3 +24,16 @@ def test_post_fake_shapes():
         xNext = torch.ops.mhc.post(x, torch.empty(2, 3, 64, dtype=torch.float16), torch.empty(2, 3, 4),
                                    torch.empty(2, 3, 4, 4))
     assert tuple(xNext.shape) == (2, 3, 4, 64) and xNext.dtype == torch.float16
+
+
+def test_post_pre_fake_shapes():
+    with FakeTensorMode():
+        x = torch.empty(2, 3, 4, 64, dtype=torch.bfloat16)
+        outs = torch.ops.mhc.post_pre(x, torch.empty(2, 3, 64, dtype=torch.bfloat16), torch.empty(2, 3, 4),
+                                      torch.empty(2, 3, 4, 4), torch.empty(24, 256), torch.empty(3),
+                                      torch.empty(24), None, 1e-6, 1e-6)
+    xNext, hIn, hPost, hRes = outs
+    assert tuple(xNext.shape) == (2, 3, 4, 64) and xNext.dtype == torch.bfloat16
+    assert tuple(hIn.shape) == (2, 3, 64) and hIn.dtype == torch.bfloat16
+    assert tuple(hPost.shape) == (2, 3, 4) and hPost.dtype == torch.float32
+    assert tuple(hRes.shape) == (2, 3, 4, 4) and hRes.dtype == torch.float32

@@ -40,3 +40,19 @@ def test_torch_post_op_matches_binding_and_opcheck():
     assert torch.equal(a, b)
     torch.library.opcheck(torch.ops.mhc.post.default, (inp["x"], hIn, hPost, hRes),
                           test_utils=("test_schema", "test_faketensor"))
+
+
+@pytest.mark.parametrize("seq", [64, 1024], ids=["two_calls", "fused_kernel"])
+def test_torch_post_pre_op_matches_binding_and_opcheck(seq):
+    """torch.ops.mhc.post_pre equals the one-shot binding (bit for bit: the same
+    path), its xNext equals the post step's, and it passes opcheck."""
+    cfg = with_shape(CONFIGS["c2"], seq=seq)
+    inp = make_inputs(cfg)
+    hIn, hPost, hRes = mp.mhc_pre(inp["x"], inp["phi"], inp["alpha"], inp["bias"], inp["gamma"])
+    args = (inp["x"], hIn, hPost, hRes, inp["phi"], inp["alpha"], inp["bias"], inp["gamma"], 1e-6, 1e-6)
+    a = torch.ops.mhc.post_pre(*args)
+    b_next, b = mp.mhc_post_pre(*args)
+    for u, v in zip(a, (b_next, *b)):
+        assert torch.equal(u, v)
+    assert torch.equal(a[0], mp.mhc_post(inp["x"], hIn, hPost, hRes))
+    torch.library.opcheck(torch.ops.mhc.post_pre.default, args, test_utils=("test_schema", "test_faketensor"))
