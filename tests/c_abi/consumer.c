@@ -5,8 +5,10 @@
  *
  *   consumer --no-gpu   ABI version, status strings and the shape rejects, which
  *                       need no device
- *   consumer            on a B200: one-shot and prepared runs of a split-K shape and
- *                       a decode shape, compared with the oracle on the same inputs
+ *   consumer            on a B200: one-shot and prepared runs of a split-K, a
+ *                       small-batch and a decode shape, and the post step fused with
+ *                       the next MhcPre (mhcPostPreRun) on each, compared with the
+ *                       oracle on the same inputs
  * Exit status 0 when every check passes. */
 #include <math.h>
 #include <stdint.h>
@@ -75,6 +77,20 @@ static int ulp_distance(uint16_t a, uint16_t b) {
     return abs(oa - ob);
 }
 
+static void check_outputs(int64_t M, int64_t n, int64_t D, const uint16_t* hin, const float* post, const float* res,
+                          const uint16_t* rin, const float* rpost, const float* rres, const char* what, int path) {
+    double err = 0.0;
+    for (int64_t i = 0; i < M * n; ++i) err = fmax(err, fabs(post[i] - rpost[i]) / fmax(1.0, fabs(rpost[i])));
+    for (int64_t i = 0; i < M * n * n; ++i) err = fmax(err, fabs(res[i] - rres[i]) / fmax(1.0, fabs(rres[i])));
+    int64_t within1 = 0;
+    for (int64_t i = 0; i < M * D; ++i) within1 += ulp_distance(hin[i], rin[i]) <= 1;
+    const double frac = (double)within1 / (double)(M * D);
+    printf("%s M=%lld n=%lld D=%lld path %d: hPost/hRes max rel err %.2e, hIn within 1 ulp %.5f\n", what,
+           (long long)M, (long long)n, (long long)D, path, err, frac);
+    CHECK(err <= 1e-4, "%s: hPost/hRes error %.3e", what, err);
+    CHECK(frac >= 0.999, "%s: hIn within 1 ulp %.5f", what, frac);
+}
+
 static void run_case(int64_t S, int64_t n, int64_t D, int32_t dtype, int32_t gamma) {
     const int64_t M = S, K = n * D, mix = n * n + 2 * n;
     uint16_t* x = malloc(sizeof(uint16_t) * M * K);
@@ -138,16 +154,42 @@ static void run_case(int64_t S, int64_t n, int64_t D, int32_t dtype, int32_t gam
                          MHC_ORACLE_ORDER_KERNEL, x, phi, alpha, bias, gamma ? g : NULL, 1e-6f, 1e-6f, rin, rpost,
                          rres, 0, M, 0) == 0,
           "oracle");
-    double err = 0.0;
-    for (int64_t i = 0; i < M * n; ++i) err = fmax(err, fabs(post[i] - rpost[i]) / fmax(1.0, fabs(rpost[i])));
-    for (int64_t i = 0; i < M * n * n; ++i) err = fmax(err, fabs(res[i] - rres[i]) / fmax(1.0, fabs(rres[i])));
-    int64_t within1 = 0;
-    for (int64_t i = 0; i < M * D; ++i) within1 += ulp_distance(hin[i], rin[i]) <= 1;
-    const double frac = (double)within1 / (double)(M * D);
-    printf("M=%lld n=%lld D=%lld path %d: hPost/hRes max rel err %.2e, hIn within 1 ulp %.5f\n", (long long)M,
-           (long long)n, (long long)D, plan.path, err, frac);
-    CHECK(err <= 1e-4, "hPost/hRes error %.3e", err);
-    CHECK(frac >= 0.999, "hIn within 1 ulp %.5f", frac);
+    check_outputs(M, n, D, hin, post, res, rin, rpost, rres, "mhcPreRun", plan.path);
+
+    /* a layer boundary: the post step with this call's hPost/hRes and a layer output y,
+       fused with the next MhcPre on the same prepared weights (mhcPostPreRun); the
+       oracle runs the post step (bit for bit) and then MhcPre on its xNext */
+    const int odt = dtype == MHC_DTYPE_BF16 ? MHC_ORACLE_BF16 : MHC_ORACLE_F16;
+    uint16_t* y = malloc(sizeof(uint16_t) * M * D);
+    for (int64_t i = 0; i < M * D; ++i)
+        y[i] = dtype == MHC_DTYPE_BF16 ? mhc_oracle_f32_to_bf16(normal()) : mhc_oracle_f32_to_f16(normal());
+    void *dy, *dxn, *dhin2, *dpost2, *dres2;
+    cudaMalloc(&dy, sizeof(uint16_t) * M * D);
+    cudaMalloc(&dxn, sizeof(uint16_t) * M * K);
+    cudaMalloc(&dhin2, sizeof(uint16_t) * M * D);
+    cudaMalloc(&dpost2, sizeof(float) * M * n);
+    cudaMalloc(&dres2, sizeof(float) * M * n * n);
+    cudaMemcpy(dy, y, sizeof(uint16_t) * M * D, cudaMemcpyHostToDevice);
+    rc = mhcPostPreRun(&d, dx, dy, dpost, dres, dxn, dalpha, dbias, dhin2, dpost2, dres2, dws, wsBytes, NULL);
+    CHECK(rc == MHC_STATUS_SUCCESS, "mhcPostPreRun: %s", mhcPreStatusString(rc));
+    cudaDeviceSynchronize();
+    CHECK(mhcPreGetDeviceStatus(&devStatus) == MHC_STATUS_SUCCESS && devStatus == 0, "device status %d", devStatus);
+    uint16_t* xn = malloc(sizeof(uint16_t) * M * K);
+    uint16_t* rxn = malloc(sizeof(uint16_t) * M * K);
+    cudaMemcpy(xn, dxn, sizeof(uint16_t) * M * K, cudaMemcpyDeviceToHost);
+    cudaMemcpy(hin2, dhin2, sizeof(uint16_t) * M * D, cudaMemcpyDeviceToHost);
+    float* post2 = malloc(sizeof(float) * M * n);
+    float* res2 = malloc(sizeof(float) * M * n * n);
+    cudaMemcpy(post2, dpost2, sizeof(float) * M * n, cudaMemcpyDeviceToHost);
+    cudaMemcpy(res2, dres2, sizeof(float) * M * n * n, cudaMemcpyDeviceToHost);
+    CHECK(mhc_post_oracle(M, (int)n, D, odt, x, y, post, res, rxn, 0) == 0, "post oracle");
+    CHECK(memcmp(xn, rxn, sizeof(uint16_t) * M * K) == 0, "mhcPostPreRun: xNext equals the post oracle bit for bit");
+    CHECK(mhc_pre_oracle(M, (int)n, D, odt, MHC_ORACLE_ORDER_KERNEL, rxn, phi, alpha, bias, gamma ? g : NULL, 1e-6f,
+                         1e-6f, rin, rpost, rres, 0, M, 0) == 0,
+          "oracle on xNext");
+    check_outputs(M, n, D, hin2, post2, res2, rin, rpost, rres, "mhcPostPreRun", plan.path);
+    free(y); free(xn); free(rxn); free(post2); free(res2);
+    cudaFree(dy); cudaFree(dxn); cudaFree(dhin2); cudaFree(dpost2); cudaFree(dres2);
 
     cudaFree(dx); cudaFree(dphi); cudaFree(dg); cudaFree(dalpha); cudaFree(dbias);
     cudaFree(dhin); cudaFree(dpost); cudaFree(dres); cudaFree(dws);

@@ -2,8 +2,9 @@
 against include/mhc_pre.h and linked with the library the way a host program that
 called the reference's aclnn pair would link it.  Without a GPU it checks the ABI
 version, status strings and shape rejects; on a B200 it also runs a split-K, a
-small-batch and a decode shape through mhcPreRun / mhcPreRunPrepared and compares
-them with the C oracle on the same inputs."""
+small-batch and a decode shape through mhcPreRun / mhcPreRunPrepared, and each
+through mhcPostPreRun (the post step fused with the next MhcPre), and compares them
+with the C oracle on the same inputs."""
 from __future__ import annotations
 
 import shutil
