@@ -389,7 +389,6 @@ class MhcPre:
         return query_plan(self.desc)
 
     def prepare(self, phi, gamma=None, stream=None):
-        torch = _torch()
         _check_weights(self.desc, self.device, phi, gamma)
         with _on_device(self.device):
             _check(lib().mhcPrePrepareWeightsEx(ctypes.byref(self.desc), _opt(), _ptr(phi), _ptr(gamma),
@@ -407,7 +406,6 @@ class MhcPre:
 
     def run_profiled(self, x, alpha, bias, out, ev_begin, ev_end, stream=None):
         """Like __call__, recording torch.cuda.Event ev_begin/ev_end around the main kernel."""
-        torch = _torch()
         _check_run(self.desc, self.device, x, alpha, bias, out)
         hIn, hPost, hRes = out
         with _on_device(self.device):
